@@ -1,0 +1,122 @@
+"""ctypes binding of ``libfna2_b200.so`` (the C ABI declared in include/fna2.h).
+
+The structures below mirror the C structs field for field.  Loading fails
+loudly when the shared library is missing: there is no fallback path.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get("FNA2_LIB", os.path.join(HERE, "libfna2_b200.so"))
+
+FNA2_ABI_VERSION = 1
+FNA2_OK = 0
+FNA2_ERR_INVALID = -1
+FNA2_ERR_CUDA = -2
+FNA2_ERR_WORKSPACE = -3
+
+EXPORTED = ["fna2_fwd", "fna2_bwd", "fna2_bwd_workspace_size", "fna2_last_error", "fna2_device_status",
+            "fna2_abi_version"]
+
+
+class Fna2Tensor(ctypes.Structure):
+    _fields_ = [("ptr", ctypes.c_void_p), ("stride", ctypes.c_int64 * 4)]
+
+
+class Fna2Problem(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int32),
+        ("seqlen_q", ctypes.c_int32),
+        ("seqlen_k", ctypes.c_int32),
+        ("total_q", ctypes.c_int32),
+        ("total_k", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("heads_kv", ctypes.c_int32),
+        ("heads_graph", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("softmax_scale", ctypes.c_float),
+        ("causal", ctypes.c_int32),
+        ("cu_seqlens_q", ctypes.c_void_p),
+        ("cu_seqlens_k", ctypes.c_void_p),
+    ]
+
+
+class Fna2FwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("prob", Fna2Problem),
+        ("q", Fna2Tensor),
+        ("k", Fna2Tensor),
+        ("v", Fna2Tensor),
+        ("r_q", Fna2Tensor),
+        ("r_k", Fna2Tensor),
+        ("graph_scale", ctypes.c_void_p),
+        ("out", Fna2Tensor),
+        ("lse", ctypes.c_void_p),
+    ]
+
+
+class Fna2BwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("prob", Fna2Problem),
+        ("q", Fna2Tensor),
+        ("k", Fna2Tensor),
+        ("v", Fna2Tensor),
+        ("r_q", Fna2Tensor),
+        ("r_k", Fna2Tensor),
+        ("graph_scale", ctypes.c_void_p),
+        ("out", Fna2Tensor),
+        ("dout", Fna2Tensor),
+        ("lse", ctypes.c_void_p),
+        ("dq", Fna2Tensor),
+        ("dk", Fna2Tensor),
+        ("dv", Fna2Tensor),
+        ("dr_q", Fna2Tensor),
+        ("dr_k", Fna2Tensor),
+        ("d_graph_scale", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+_lib: Optional[ctypes.CDLL] = None
+
+
+def load(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load the library once; raise if it is missing or of another ABI."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise RuntimeError(
+            f"libfna2_b200.so not found at {path}; build it with `python -m fna2_b200.build` "
+            "(there is no CPU or fallback implementation)")
+    lib = ctypes.CDLL(path)
+    lib.fna2_fwd.argtypes = [ctypes.POINTER(Fna2FwdArgs), ctypes.c_void_p]
+    lib.fna2_fwd.restype = ctypes.c_int
+    lib.fna2_bwd.argtypes = [ctypes.POINTER(Fna2BwdArgs), ctypes.c_void_p]
+    lib.fna2_bwd.restype = ctypes.c_int
+    lib.fna2_bwd_workspace_size.argtypes = [ctypes.POINTER(Fna2Problem)]
+    lib.fna2_bwd_workspace_size.restype = ctypes.c_size_t
+    lib.fna2_last_error.argtypes = []
+    lib.fna2_last_error.restype = ctypes.c_char_p
+    lib.fna2_device_status.argtypes = [ctypes.c_int]
+    lib.fna2_device_status.restype = ctypes.c_int
+    lib.fna2_abi_version.argtypes = []
+    lib.fna2_abi_version.restype = ctypes.c_int
+    v = lib.fna2_abi_version()
+    if v != FNA2_ABI_VERSION:
+        raise RuntimeError(f"libfna2_b200.so ABI {v} != expected {FNA2_ABI_VERSION}; rebuild it")
+    _lib = lib
+    return lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != FNA2_OK:
+        msg = load().fna2_last_error().decode(errors="replace")
+        kind = {FNA2_ERR_INVALID: "invalid argument", FNA2_ERR_CUDA: "CUDA error",
+                FNA2_ERR_WORKSPACE: "workspace too small"}.get(rc, f"error {rc}")
+        raise RuntimeError(f"{what}: {kind}: {msg}")

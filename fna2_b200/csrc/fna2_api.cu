@@ -1,0 +1,316 @@
+// extern "C" entry points of libfna2_b200.so (declared in include/fna2.h):
+// argument validation, TMA tensor-map construction and kernel launches.
+//
+// The whole library is one translation unit (the kernel sources are included
+// below) so the device-side watchdog flag needs no relocatable device code.
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/fna2.h"
+#include "fna2_kernels.cuh"
+#include "ptx.cuh"
+
+#include "fna2_bwd.cu"
+#include "fna2_fwd.cu"
+
+namespace fna2 {
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define FNA2_CHECK(cond, ...) \
+  do {                        \
+    if (!(cond)) return fail(FNA2_ERR_INVALID, __VA_ARGS__); \
+  } while (0)
+
+#define FNA2_CUDA(call)                                                                     \
+  do {                                                                                      \
+    cudaError_t e_ = (call);                                                                \
+    if (e_ != cudaSuccess) return fail(FNA2_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)
+
+// Driver-API calls (tensor-map encoding) need the device's primary context to
+// be current on the calling thread; PyTorch's autograd worker threads may not
+// have bound it yet.  cudaFree(nullptr) makes the runtime bind it.
+int ensure_context() {
+  thread_local bool bound = false;
+  if (!bound) {
+    cudaError_t e = cudaFree(nullptr);
+    if (e != cudaSuccess) return fail(FNA2_ERR_CUDA, "cudaFree(nullptr): %s", cudaGetErrorString(e));
+    bound = true;
+  }
+  return FNA2_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 4-D bf16 tensor map over (col, row, head, batch) with a (box0 x box1 x 1 x 1) box.
+int make_map(CUtensorMap* m, const void* ptr, uint64_t cols, uint64_t rows, uint64_t heads, uint64_t batch,
+             int64_t s_row, int64_t s_head, int64_t s_batch, uint32_t box0, uint32_t box1,
+             CUtensorMapSwizzle swz, const char* what) {
+  if (int rc = ensure_context()) return rc;
+  auto enc = encode_fn();
+  FNA2_CHECK(enc != nullptr, "cuTensorMapEncodeTiled is unavailable from the driver");
+  // size-1 dimensions may carry any stride in PyTorch; give TMA a legal one
+  if (rows <= 1 && (s_row <= 0 || (s_row * 2) % 16)) s_row = 8;
+  if (heads <= 1 && (s_head <= 0 || (s_head * 2) % 16)) s_head = s_row * static_cast<int64_t>(rows ? rows : 1);
+  if (batch <= 1 && (s_batch <= 0 || (s_batch * 2) % 16)) s_batch = s_head * static_cast<int64_t>(heads ? heads : 1);
+  cuuint64_t dims[4] = {cols, rows ? rows : 1, heads ? heads : 1, batch ? batch : 1};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(s_row) * 2, static_cast<cuuint64_t>(s_head) * 2,
+                           static_cast<cuuint64_t>(s_batch) * 2};
+  cuuint32_t box[4] = {box0, box1, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  FNA2_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (%d) for %s", static_cast<int>(r), what);
+  return FNA2_OK;
+}
+
+int check_tensor(const Fna2Tensor& t, const char* name, bool varlen) {
+  FNA2_CHECK(t.ptr != nullptr, "%s: null pointer", name);
+  FNA2_CHECK((reinterpret_cast<uintptr_t>(t.ptr) & 15u) == 0, "%s: base pointer must be 16-byte aligned", name);
+  FNA2_CHECK(t.stride[3] == 1, "%s: column stride must be 1 (got %lld)", name, (long long)t.stride[3]);
+  for (int i = varlen ? 1 : 0; i < 3; ++i)
+    FNA2_CHECK(t.stride[i] >= 0 && (t.stride[i] % 8) == 0,
+               "%s: stride[%d] = %lld must be a non-negative multiple of 8 elements (16 bytes)", name, i,
+               (long long)t.stride[i]);
+  return FNA2_OK;
+}
+
+struct Shape {
+  bool varlen;
+  int B, Sq, Sk, Tq, Tk, H, HKV, HG, D, r, RP;
+  int rows_q() const { return varlen ? Tq : Sq; }
+  int rows_k() const { return varlen ? Tk : Sk; }
+  int batch_dim() const { return varlen ? 1 : B; }
+};
+
+int check_problem(const Fna2Problem& p, Shape* s) {
+  s->varlen = p.cu_seqlens_q != nullptr;
+  FNA2_CHECK((p.cu_seqlens_q == nullptr) == (p.cu_seqlens_k == nullptr),
+             "cu_seqlens_q and cu_seqlens_k must both be given or both be NULL");
+  FNA2_CHECK(p.batch >= 0 && p.seqlen_q >= 0 && p.seqlen_k >= 0, "negative batch or sequence length");
+  FNA2_CHECK(p.head_dim == 64 || p.head_dim == 128, "head_dim must be 64 or 128 (got %d)", p.head_dim);
+  FNA2_CHECK(p.heads > 0 && p.heads_kv > 0 && p.heads % p.heads_kv == 0,
+             "heads (%d) must be a positive multiple of heads_kv (%d)", p.heads, p.heads_kv);
+  FNA2_CHECK(p.heads_graph >= 0 && p.heads_graph <= p.heads, "heads_graph (%d) must be in [0, heads=%d]",
+             p.heads_graph, p.heads);
+  FNA2_CHECK(p.heads <= 65535 && p.batch <= 65535, "heads and batch/sequence count must be <= 65535");
+  if (p.heads_graph > 0)
+    FNA2_CHECK(p.rank > 0 && p.rank <= 32 && p.rank % 8 == 0, "rank must be 8, 16, 24 or 32 (got %d)", p.rank);
+  FNA2_CHECK(p.softmax_scale > 0.f, "softmax_scale must be positive");
+  if (s->varlen) FNA2_CHECK(p.total_q >= 0 && p.total_k >= 0, "negative total_q/total_k");
+  s->B = p.batch;
+  s->Sq = p.seqlen_q;
+  s->Sk = p.seqlen_k;
+  s->Tq = p.total_q;
+  s->Tk = p.total_k;
+  s->H = p.heads;
+  s->HKV = p.heads_kv;
+  s->HG = p.heads_graph;
+  s->D = p.head_dim;
+  s->r = p.heads_graph > 0 ? p.rank : 16;
+  s->RP = s->r <= 16 ? 16 : 32;
+  if (!s->varlen) FNA2_CHECK(p.seqlen_q == p.seqlen_k, "dense problems need seqlen_q == seqlen_k");
+  return FNA2_OK;
+}
+
+ProblemDev to_dev(const Fna2Problem& p, const Shape& s) {
+  ProblemDev d;
+  d.heads = s.H;
+  d.heads_kv = s.HKV;
+  d.heads_graph = s.HG;
+  d.head_dim = s.D;
+  d.rank = s.r;
+  d.seqlen_q = s.Sq;
+  d.seqlen_k = s.Sk;
+  d.varlen = s.varlen ? 1 : 0;
+  d.causal = s.varlen ? 1 : (p.causal ? 1 : 0);
+  d.cu_q = p.cu_seqlens_q;
+  d.cu_k = p.cu_seqlens_k;
+  d.scale = p.softmax_scale;
+  d.scale_log2 = p.softmax_scale * kLog2e;
+  d.gs = nullptr;
+  return d;
+}
+
+// Tensor maps shared by forward and backward: Q/K/V (and dO) with 64-column
+// SW128 boxes of 128 rows, R_q/R_k with r_pad-column boxes (zero-filled past r).
+int map_qkv(CUtensorMap* m, const Fna2Tensor& t, const Shape& s, int rows, int heads, const char* what) {
+  return make_map(m, t.ptr, s.D, rows, heads, s.batch_dim(), t.stride[2], t.stride[1], t.stride[0], 64, 128,
+                  CU_TENSOR_MAP_SWIZZLE_128B, what);
+}
+int map_r(CUtensorMap* m, const Fna2Tensor& t, const Shape& s, int rows, const char* what) {
+  return make_map(m, t.ptr, s.r, rows, s.HG, s.batch_dim(), t.stride[2], t.stride[1], t.stride[0], s.RP, 128,
+                  s.RP == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B, what);
+}
+
+}  // namespace
+}  // namespace fna2
+
+using namespace fna2;
+
+extern "C" int fna2_abi_version(void) { return FNA2_ABI_VERSION; }
+
+extern "C" const char* fna2_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" int fna2_device_status(int reset) {
+  int v = 0;
+  FNA2_CUDA(cudaDeviceSynchronize());
+  FNA2_CUDA(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)));
+  if (reset) {
+    int z = 0;
+    FNA2_CUDA(cudaMemcpyToSymbol(g_device_error, &z, sizeof(int)));
+  }
+  return v;
+}
+
+extern "C" int fna2_fwd(const Fna2FwdArgs* a, void* stream) {
+  g_last_error.clear();
+  FNA2_CHECK(a != nullptr, "null args");
+  Shape s;
+  if (int rc = check_problem(a->prob, &s)) return rc;
+  if (s.B == 0 || s.Sq == 0 || s.H == 0) return FNA2_OK;
+  if (int rc = check_tensor(a->q, "q", s.varlen)) return rc;
+  if (int rc = check_tensor(a->k, "k", s.varlen)) return rc;
+  if (int rc = check_tensor(a->v, "v", s.varlen)) return rc;
+  if (int rc = check_tensor(a->out, "out", s.varlen)) return rc;
+  FNA2_CHECK(a->lse != nullptr, "lse: null pointer");
+  if (s.HG > 0) {
+    if (int rc = check_tensor(a->r_q, "r_q", s.varlen)) return rc;
+    if (int rc = check_tensor(a->r_k, "r_k", s.varlen)) return rc;
+    FNA2_CHECK(a->graph_scale != nullptr, "graph_scale: null pointer");
+  }
+  CUtensorMap tq, tk, tv, trq, trk;
+  if (int rc = map_qkv(&tq, a->q, s, s.rows_q(), s.H, "q")) return rc;
+  if (int rc = map_qkv(&tk, a->k, s, s.rows_k(), s.HKV, "k")) return rc;
+  if (int rc = map_qkv(&tv, a->v, s, s.rows_k(), s.HKV, "v")) return rc;
+  if (s.HG > 0) {
+    if (int rc = map_r(&trq, a->r_q, s, s.rows_q(), "r_q")) return rc;
+    if (int rc = map_r(&trk, a->r_k, s, s.rows_k(), "r_k")) return rc;
+  } else {
+    trq = tq;  // never dereferenced: no graph heads
+    trk = tk;
+  }
+  FwdParams p;
+  p.prob = to_dev(a->prob, s);
+  p.prob.gs = a->graph_scale;
+  p.out = static_cast<__nv_bfloat16*>(a->out.ptr);
+  p.o_sb = s.varlen ? 0 : a->out.stride[0];
+  p.o_sh = a->out.stride[1];
+  p.o_sr = a->out.stride[2];
+  p.lse = a->lse;
+  p.lse_sbh = s.rows_q();
+  p.n_mblocks = (s.Sq + kBlockM - 1) / kBlockM;
+  FNA2_CUDA(launch_fwd(s.D, s.RP, tq, tk, tv, trq, trk, p, s.H, s.B, static_cast<cudaStream_t>(stream)));
+  return FNA2_OK;
+}
+
+extern "C" size_t fna2_bwd_workspace_size(const Fna2Problem* prob) {
+  if (!prob) return 0;
+  Shape s;
+  if (check_problem(*prob, &s)) return 0;
+  return bwd_workspace_bytes(s.batch_dim(), s.H, s.HG, s.rows_q());
+}
+
+extern "C" int fna2_bwd(const Fna2BwdArgs* a, void* stream) {
+  g_last_error.clear();
+  FNA2_CHECK(a != nullptr, "null args");
+  Shape s;
+  if (int rc = check_problem(a->prob, &s)) return rc;
+  if (s.B == 0 || s.Sq == 0) return FNA2_OK;
+  const char* names[] = {"q", "k", "v", "out", "dout", "dq", "dk", "dv"};
+  const Fna2Tensor* ts[] = {&a->q, &a->k, &a->v, &a->out, &a->dout, &a->dq, &a->dk, &a->dv};
+  for (int i = 0; i < 8; ++i)
+    if (int rc = check_tensor(*ts[i], names[i], s.varlen)) return rc;
+  FNA2_CHECK(a->lse != nullptr, "lse: null pointer");
+  if (s.HG > 0) {
+    if (int rc = check_tensor(a->r_q, "r_q", s.varlen)) return rc;
+    if (int rc = check_tensor(a->r_k, "r_k", s.varlen)) return rc;
+    if (int rc = check_tensor(a->dr_q, "dr_q", s.varlen)) return rc;
+    if (int rc = check_tensor(a->dr_k, "dr_k", s.varlen)) return rc;
+    FNA2_CHECK(a->graph_scale != nullptr && a->d_graph_scale != nullptr, "graph_scale/d_graph_scale: null");
+  }
+  const size_t need = bwd_workspace_bytes(s.batch_dim(), s.H, s.HG, s.rows_q());
+  if (a->workspace_bytes < need || (need && a->workspace == nullptr))
+    return fail(FNA2_ERR_WORKSPACE, "workspace too small: %zu < %zu bytes", a->workspace_bytes, need);
+  FNA2_CHECK((reinterpret_cast<uintptr_t>(a->workspace) & 255u) == 0, "workspace must be 256-byte aligned");
+
+  CUtensorMap tq, tk, tv, tdo, trq, trk;
+  if (int rc = map_qkv(&tq, a->q, s, s.rows_q(), s.H, "q")) return rc;
+  if (int rc = map_qkv(&tk, a->k, s, s.rows_k(), s.HKV, "k")) return rc;
+  if (int rc = map_qkv(&tv, a->v, s, s.rows_k(), s.HKV, "v")) return rc;
+  if (int rc = map_qkv(&tdo, a->dout, s, s.rows_q(), s.H, "dout")) return rc;
+  if (s.HG > 0) {
+    if (int rc = map_r(&trq, a->r_q, s, s.rows_q(), "r_q")) return rc;
+    if (int rc = map_r(&trk, a->r_k, s, s.rows_k(), "r_k")) return rc;
+  } else {
+    trq = tq;
+    trk = tk;
+  }
+  BwdParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.prob = to_dev(a->prob, s);
+  p.prob.gs = a->graph_scale;
+  auto set3 = [&](const Fna2Tensor& t, int64_t* sb, int64_t* sh, int64_t* sr) {
+    *sb = s.varlen ? 0 : t.stride[0];
+    *sh = t.stride[1];
+    *sr = t.stride[2];
+  };
+  p.out = static_cast<const __nv_bfloat16*>(a->out.ptr);
+  set3(a->out, &p.o_sb, &p.o_sh, &p.o_sr);
+  p.dout = static_cast<const __nv_bfloat16*>(a->dout.ptr);
+  set3(a->dout, &p.do_sb, &p.do_sh, &p.do_sr);
+  p.lse = a->lse;
+  p.lse_sbh = s.rows_q();
+  p.dq = static_cast<__nv_bfloat16*>(a->dq.ptr);
+  set3(a->dq, &p.dq_sb, &p.dq_sh, &p.dq_sr);
+  p.dk = static_cast<__nv_bfloat16*>(a->dk.ptr);
+  set3(a->dk, &p.dk_sb, &p.dk_sh, &p.dk_sr);
+  p.dv = static_cast<__nv_bfloat16*>(a->dv.ptr);
+  set3(a->dv, &p.dv_sb, &p.dv_sh, &p.dv_sr);
+  if (s.HG > 0) {
+    p.drq = static_cast<__nv_bfloat16*>(a->dr_q.ptr);
+    set3(a->dr_q, &p.drq_sb, &p.drq_sh, &p.drq_sr);
+    p.drk = static_cast<__nv_bfloat16*>(a->dr_k.ptr);
+    set3(a->dr_k, &p.drk_sb, &p.drk_sh, &p.drk_sr);
+    p.rq = static_cast<const __nv_bfloat16*>(a->r_q.ptr);
+    set3(a->r_q, &p.rq_sb, &p.rq_sh, &p.rq_sr);
+    p.dgs = a->d_graph_scale;
+  }
+  p.total_q_rows = s.rows_q();
+  p.total_k_rows = s.rows_k();
+  p.batch = s.B;
+  p.n_mblocks = (s.Sq + kBlockM - 1) / kBlockM;
+  p.n_nblocks = (s.Sk + kBlockN - 1) / kBlockN;
+  bwd_set_workspace(&p, a->workspace, s.batch_dim(), s.H, s.rows_q());
+  FNA2_CUDA(launch_bwd(s.D, s.RP, tq, tk, tv, tdo, trq, trk, p, static_cast<cudaStream_t>(stream)));
+  return FNA2_OK;
+}

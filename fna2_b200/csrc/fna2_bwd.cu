@@ -1,0 +1,838 @@
+// FNA2 backward on sm_100a.
+//
+// Reference semantics: FNA2/flash_naylis_attn.py:356-693 (dense) and
+// :900-1208 (varlen): Delta = rowsum(dO*O) (:381), P = exp(S - LSE) (:518),
+// dS = P*(dP - Delta) (:523), dV = P^T dO (:527), dK = scale*dS^T Q (:529),
+// dR_k = gs*dS^T R_q (:535), dQ = scale*dS K (:679), dR_q = gs*dS R_k (:683),
+// d_gs[h] = sum(dS * R_q R_k^T) (:537-538).  d_gs is formed here from the
+// identity d_gs[h] = sum_i <R_q[i], (dS R_k)[i]>, so R_q R_k^T is never
+// recomputed for it.
+//
+// Three launches:
+//   fna2_bwd_pre_kernel   Delta and the LSE in log2 units into the workspace;
+//                         zeroes d_gs and (varlen) gradient rows that belong
+//                         to no sequence, as the reference's zeros_like does.
+//   fna2_bwd_dkdv_kernel  one CTA per (128-row key tile, KV head, sequence),
+//                         looping over the query heads of the GQA group and
+//                         the causally visible query tiles.  TMEM: dV, dK
+//                         accumulators; S^T = K Q^T + R_k R~_q^T and
+//                         dP^T = V dO^T per step; the softmax warps write P^T
+//                         and dS^T back into TMEM as bf16 and the TS-form MMAs
+//                         dV += P^T dO, dK += dS^T Q, dR_k-tile = dS^T R~_q
+//                         read them from there.  No dK/dV atomics.
+//   fna2_bwd_dq_kernel    one CTA per (128-row query tile, head, sequence),
+//                         looping over the causally visible key tiles:
+//                         S, dP, dS (bf16 into TMEM), dQ += dS K and
+//                         dR_q += dS R_k (TS-form), then d_gs via one atomic
+//                         per warp.
+// R~_q = R_q * gs/scale is staged in shared memory so the bias is one extra
+// K-slice (K = r_pad) of the score MMA; dR_k = scale * dS^T R~_q follows.
+#include "fna2_kernels.cuh"
+#include "ptx.cuh"
+
+namespace fna2 {
+
+inline size_t bwd_ws_align(size_t x) { return (x + 255) & ~size_t(255); }
+
+inline size_t bwd_workspace_bytes(int batch_dim, int H, int /*HG*/, int rows) {
+  const size_t n = static_cast<size_t>(batch_dim) * H * rows;
+  return 2 * bwd_ws_align(n * sizeof(float));
+}
+
+inline void bwd_set_workspace(BwdParams* p, void* ws, int batch_dim, int H, int rows) {
+  const size_t n = static_cast<size_t>(batch_dim) * H * rows;
+  p->ws_lse2 = static_cast<float*>(ws);
+  p->ws_delta = reinterpret_cast<float*>(static_cast<char*>(ws) + bwd_ws_align(n * sizeof(float)));
+  p->ws_sbh = rows;
+}
+
+__device__ __forceinline__ void zero_row(__nv_bfloat16* row, int n) {
+  uint4 z = make_uint4(0, 0, 0, 0);
+  for (int c = 0; c < n; c += 8) *reinterpret_cast<uint4*>(row + c) = z;
+}
+
+// ---------------------------------------------------------------------------
+// pre-pass: Delta = rowsum(dO*O), lse2 = LSE*log2(e)
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(128) fna2_bwd_pre_kernel(const BwdParams p) {
+  const ProblemDev& P = p.prob;
+  const int h = blockIdx.y;
+  const int bz = blockIdx.z;
+  const int row = blockIdx.x * 128 + threadIdx.x;
+  if (blockIdx.x == 0 && h == 0 && bz == 0 && p.dgs != nullptr && static_cast<int>(threadIdx.x) < P.heads_graph)
+    p.dgs[threadIdx.x] = 0.f;
+  if (row < p.total_q_rows) {
+    const __nv_bfloat16* o = p.out + bz * p.o_sb + h * p.o_sh + static_cast<int64_t>(row) * p.o_sr;
+    const __nv_bfloat16* g = p.dout + bz * p.do_sb + h * p.do_sh + static_cast<int64_t>(row) * p.do_sr;
+    float acc = 0.f;
+#pragma unroll
+    for (int c = 0; c < D; c += 8) {
+      const uint4 a = *reinterpret_cast<const uint4*>(o + c);
+      const uint4 b = *reinterpret_cast<const uint4*>(g + c);
+      const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&b);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 x = __bfloat1622float2(a2[i]);
+        const float2 y = __bfloat1622float2(b2[i]);
+        acc = fmaf(x.x, y.x, acc);
+        acc = fmaf(x.y, y.y, acc);
+      }
+    }
+    const int64_t idx = (static_cast<int64_t>(bz) * P.heads + h) * p.ws_sbh + row;
+    p.ws_delta[idx] = acc;
+    p.ws_lse2[idx] = p.lse[(static_cast<int64_t>(bz) * P.heads + h) * p.lse_sbh + row] * kLog2e;
+  }
+  if (P.varlen) {
+    // rows outside [cu[0], cu[N]) are not owned by any tile: zero them
+    const int q_lo = __ldg(P.cu_q), q_hi = __ldg(P.cu_q + p.batch);
+    const int k_lo = __ldg(P.cu_k), k_hi = __ldg(P.cu_k + p.batch);
+    if (row < p.total_q_rows && (row < q_lo || row >= q_hi)) {
+      zero_row(p.dq + h * p.dq_sh + static_cast<int64_t>(row) * p.dq_sr, D);
+      if (h < P.heads_graph) zero_row(p.drq + h * p.drq_sh + static_cast<int64_t>(row) * p.drq_sr, P.rank);
+    }
+    if (row < p.total_k_rows && (row < k_lo || row >= k_hi)) {
+      if (h < P.heads_kv) {
+        zero_row(p.dk + h * p.dk_sh + static_cast<int64_t>(row) * p.dk_sr, D);
+        zero_row(p.dv + h * p.dv_sh + static_cast<int64_t>(row) * p.dv_sr, D);
+      }
+      if (h < P.heads_graph) zero_row(p.drk + h * p.drk_sh + static_cast<int64_t>(row) * p.drk_sr, P.rank);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// shared helpers
+// ---------------------------------------------------------------------------
+template <int RP>
+__device__ __forceinline__ void scale_rows_inplace(uint8_t* base, int row, float f) {
+  uint4* rrow = reinterpret_cast<uint4*>(base + row * RP * 2);
+#pragma unroll
+  for (int u = 0; u < RP / 8; ++u) {
+    uint4 w = rrow[u];
+    uint32_t* e = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f2 = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&e[i]));
+      e[i] = pack_bf16(f2.x * f, f2.y * f);
+    }
+    rrow[u] = w;
+  }
+}
+
+// Store 32 fp32 values (scaled) as bf16 to a row (16-byte aligned).
+__device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const uint32_t* v, float f) {
+  uint4 w[4];
+  uint32_t* wp = reinterpret_cast<uint32_t*>(w);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) wp[i] = pack_bf16(__uint_as_float(v[2 * i]) * f, __uint_as_float(v[2 * i + 1]) * f);
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) d4[i] = w[i];
+}
+
+__device__ __forceinline__ uint32_t r_layout_of(int rp) {
+  return rp == 16 ? kSwizzle32B : (rp == 32 ? kSwizzle64B : kSwizzle128B);
+}
+
+// ---------------------------------------------------------------------------
+// dK / dV / dR_k  (KV-stationary)
+// ---------------------------------------------------------------------------
+template <int D, int RP>
+struct DkdvSmem {
+  static constexpr int kTile = 128 * D * 2;
+  static constexpr int kR = 128 * RP * 2;
+  static constexpr int kChunk = 128 * 128;
+  static constexpr int align(int x) { return (x + 1023) & ~1023; }
+  static constexpr int oK = 0;
+  static constexpr int oV = align(oK + kTile);
+  static constexpr int oRk = align(oV + kTile);
+  static constexpr int oQ0 = align(oRk + kR);
+  static constexpr int oQ1 = align(oQ0 + kTile);
+  static constexpr int oDo0 = align(oQ1 + kTile);
+  static constexpr int oDo1 = align(oDo0 + kTile);
+  static constexpr int oRq0 = align(oDo1 + kTile);
+  static constexpr int oRq1 = align(oRq0 + kR);
+  static constexpr int oVec = align(oRq1 + kR);  // [2 stages][lse2 128 | delta 128] floats
+  static constexpr int oBar = oVec + 2 * 256 * 4;
+  static constexpr int kNumBars = 16;
+  static constexpr int oMisc = oBar + kNumBars * 8;
+  static constexpr int kTotal = oMisc + 16 + 1024;
+};
+
+enum DkdvBar {
+  kAKV = 0,
+  kARkFull = 1,
+  kARkEmpty = 2,
+  kAQFull = 3,    // +stage
+  kAQEmpty = 5,   // +stage
+  kAPrep = 7,     // +stage
+  kAStFull = 9,
+  kAPReady = 10,
+  kADrk = 11,
+  kATmemFree = 12,
+  kAAllDone = 13,
+};
+
+template <int D, int RP>
+__global__ void __launch_bounds__(224, 1)
+    fna2_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDo,
+                         const __grid_constant__ CUtensorMap tmRq, const __grid_constant__ CUtensorMap tmRk,
+                         const BwdParams p) {
+  using L = DkdvSmem<D, RP>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::oBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::oMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::oMisc + 4);
+  float* vec = reinterpret_cast<float*>(smem + L::oVec);
+
+  const ProblemDev& P = p.prob;
+  const int n_blk = blockIdx.x;
+  const int hk = blockIdx.y;
+  const SeqInfo si = seq_info(P, blockIdx.z);
+  const int n0 = n_blk * kBlockN;
+  if (n0 >= si.len_k) return;
+  const int g = P.heads / P.heads_kv;
+  const int gh = max(0, min(g, P.heads_graph - hk * g));  // graph heads of this group (a prefix)
+  const int m_start = P.causal ? n_blk : 0;
+  const int m_end = (si.len_q + kBlockM - 1) / kBlockM;
+  const int n_it = max(0, m_end - m_start);
+  const int total_it = g * n_it;
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int tid = threadIdx.x;
+  const float scale = P.scale;
+
+  if (total_it == 0) {
+    // no query sees this key tile: dK = dV = dR_k = 0
+    if (tid < kBlockN && n0 + tid < si.len_k) {
+      const int64_t row = si.k_start + n0 + tid;
+      zero_row(p.dk + si.b * p.dk_sb + hk * p.dk_sh + row * p.dk_sr, D);
+      zero_row(p.dv + si.b * p.dv_sb + hk * p.dv_sh + row * p.dv_sr, D);
+      for (int e = 0; e < gh; ++e)
+        zero_row(p.drk + si.b * p.drk_sb + (hk * g + e) * p.drk_sh + row * p.drk_sr, P.rank);
+    }
+    return;
+  }
+
+  if (tid == 0) {
+    mbar_init(&bars[kAKV], 1);
+    mbar_init(&bars[kARkFull], 1);
+    mbar_init(&bars[kARkEmpty], 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars[kAQFull + s], 1);
+      mbar_init(&bars[kAQEmpty + s], 1);
+      mbar_init(&bars[kAPrep + s], 32);
+    }
+    mbar_init(&bars[kAStFull], 1);
+    mbar_init(&bars[kAPReady], 128);
+    mbar_init(&bars[kADrk], 1);
+    mbar_init(&bars[kATmemFree], 128);
+    mbar_init(&bars[kAAllDone], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM columns
+  const uint32_t tDV = tmem + 0, tDK = tmem + 128, tS = tmem + 256, tDP = tmem + 384, tDRK = tmem + 256 + 64;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmDo);
+      const int krow = si.k_start + n0;
+      mbar_expect_tx(&bars[kAKV], 2 * L::kTile);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        tma_load_4d(smem + L::oK + c * L::kChunk, &tmK, &bars[kAKV], c * 64, krow, hk, si.b);
+        tma_load_4d(smem + L::oV + c * L::kChunk, &tmV, &bars[kAKV], c * 64, krow, hk, si.b);
+      }
+      int it = 0;
+      bool ok = true;
+      for (int e = 0; ok && e < g; ++e) {
+        const int h = hk * g + e;
+        const bool graph = e < gh;
+        if (graph) {
+          if (e > 0 && !mbar_wait(&bars[kARkEmpty], (e - 1) & 1, abort_flag, 401)) break;
+          mbar_expect_tx(&bars[kARkFull], L::kR);
+          tma_load_4d(smem + L::oRk, &tmRk, &bars[kARkFull], 0, krow, h, si.b);
+        }
+        for (int mi = 0; mi < n_it; ++mi, ++it) {
+          const int s = it & 1;
+          if (it >= 2 && !mbar_wait(&bars[kAQEmpty + s], ((it >> 1) - 1) & 1, abort_flag, 402)) {
+            ok = false;
+            break;
+          }
+          const int qrow = si.q_start + (m_start + mi) * kBlockM;
+          mbar_expect_tx(&bars[kAQFull + s], 2 * L::kTile + (graph ? L::kR : 0));
+#pragma unroll
+          for (int c = 0; c < D / 64; ++c) {
+            tma_load_4d(smem + (s ? L::oQ1 : L::oQ0) + c * L::kChunk, &tmQ, &bars[kAQFull + s], c * 64, qrow, h,
+                        si.b);
+            tma_load_4d(smem + (s ? L::oDo1 : L::oDo0) + c * L::kChunk, &tmDo, &bars[kAQFull + s], c * 64, qrow,
+                        h, si.b);
+          }
+          if (graph) tma_load_4d(smem + (s ? L::oRq1 : L::oRq0), &tmRq, &bars[kAQFull + s], 0, qrow, h, si.b);
+        }
+      }
+    }
+  } else if (warp == 6) {
+    // ------------------------------------------------------------ prep: lse2/Delta rows, R~_q
+    int it = 0;
+    bool ok = true;
+    for (int e = 0; ok && e < g; ++e) {
+      const int h = hk * g + e;
+      const bool graph = e < gh;
+      const float f = graph ? __ldg(P.gs + h) / scale : 0.f;
+      const int64_t wbase = (static_cast<int64_t>(si.b) * P.heads + h) * p.ws_sbh + si.q_start;
+      for (int mi = 0; mi < n_it; ++mi, ++it) {
+        const int s = it & 1;
+        const int m0 = (m_start + mi) * kBlockM;
+        float* lv = vec + s * 256;
+        if (!mbar_wait(&bars[kAQFull + s], (it >> 1) & 1, abort_flag, 601)) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int t = lane + 32 * u;
+          const bool valid = m0 + t < si.len_q;
+          lv[t] = valid ? p.ws_lse2[wbase + m0 + t] : 0.f;
+          lv[128 + t] = valid ? p.ws_delta[wbase + m0 + t] : 0.f;
+          if (graph) scale_rows_inplace<RP>(smem + (s ? L::oRq1 : L::oRq0), t, f);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&bars[kAPrep + s]);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_st = make_idesc_bf16(128, 128, 0, 0);    // S^T, dP^T
+      constexpr uint32_t idesc_acc = make_idesc_bf16(128, D, 0, 1);     // dV, dK (A in TMEM, B MN-major)
+      constexpr uint32_t idesc_drk = make_idesc_bf16(128, RP, 0, 1);    // dR_k tile
+      const uint32_t r_layout = r_layout_of(RP);
+      const uint32_t r_sbo = 8 * RP * 2;
+      const uint32_t sK = smem_u32(smem + L::oK), sV = smem_u32(smem + L::oV), sRk = smem_u32(smem + L::oRk);
+      bool ok = mbar_wait(&bars[kAKV], 0, abort_flag, 501);
+      int it = 0;
+      for (int e = 0; ok && e < g; ++e) {
+        const bool graph = e < gh;
+        if (graph && !mbar_wait(&bars[kARkFull], e & 1, abort_flag, 502)) break;
+        for (int mi = 0; mi < n_it; ++mi, ++it) {
+          const int s = it & 1;
+          const uint32_t sQ = smem_u32(smem + (s ? L::oQ1 : L::oQ0));
+          const uint32_t sDo = smem_u32(smem + (s ? L::oDo1 : L::oDo0));
+          const uint32_t sRq = smem_u32(smem + (s ? L::oRq1 : L::oRq0));
+          if (!mbar_wait(&bars[kAQFull + s], (it >> 1) & 1, abort_flag, 503) ||
+              !mbar_wait(&bars[kAPrep + s], (it >> 1) & 1, abort_flag, 504) ||
+              (it > 0 && !mbar_wait(&bars[kATmemFree], (it - 1) & 1, abort_flag, 505))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // S^T = K Q^T (+ R_k R~_q^T), dP^T = V dO^T
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * L::kChunk + (kk & 3) * 32;
+            mma_ss(tS, make_sdesc(sK + off, 16, 1024, kSwizzle128B), make_sdesc(sQ + off, 16, 1024, kSwizzle128B),
+                   idesc_st, kk > 0);
+          }
+          if (graph) {
+#pragma unroll
+            for (int kk = 0; kk < RP / 16; ++kk)
+              mma_ss(tS, make_sdesc(sRk + kk * 32, 16, r_sbo, r_layout), make_sdesc(sRq + kk * 32, 16, r_sbo, r_layout),
+                     idesc_st, 1);
+          }
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * L::kChunk + (kk & 3) * 32;
+            mma_ss(tDP, make_sdesc(sV + off, 16, 1024, kSwizzle128B), make_sdesc(sDo + off, 16, 1024, kSwizzle128B),
+                   idesc_st, kk > 0);
+          }
+          mma_commit(&bars[kAStFull]);
+          if (!mbar_wait(&bars[kAPReady], it & 1, abort_flag, 506)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // dV += P^T dO ; dK += dS^T Q   (K = 128 query rows, 8 steps of 16)
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_ts(tDV, tS + kk * 8, make_sdesc(sDo + kk * 2048, L::kChunk, 1024, kSwizzle128B), idesc_acc,
+                   (it > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_ts(tDK, tDP + kk * 8, make_sdesc(sQ + kk * 2048, L::kChunk, 1024, kSwizzle128B), idesc_acc,
+                   (it > 0 || kk > 0) ? 1u : 0u);
+          if (graph) {
+            // dR_k tile = dS^T R~_q  (B MN-major: r_pad contiguous, rows of RP*2 bytes)
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              mma_ts(tDRK, tDP + kk * 8, make_sdesc(sRq + kk * 16 * RP * 2, 16, r_sbo, r_layout), idesc_drk,
+                     kk > 0 ? 1u : 0u);
+            mma_commit(&bars[kADrk]);
+          }
+          mma_commit(&bars[kAQEmpty + s]);
+          if (graph && mi == n_it - 1) mma_commit(&bars[kARkEmpty]);
+        }
+      }
+      if (ok) mma_commit(&bars[kAAllDone]);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax-gradient warps 0-3 (key rows)
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const int kv_local = n0 + tid;
+    const bool kv_valid = kv_local < si.len_k;
+    const float sl2 = P.scale_log2;
+    const int64_t krow = si.k_start + kv_local;
+    float drk_acc[RP];
+#pragma unroll
+    for (int i = 0; i < RP; ++i) drk_acc[i] = 0.f;
+    int it = 0, git = 0;
+    bool ok = true;
+    for (int e = 0; ok && e < g; ++e) {
+      const int h = hk * g + e;
+      const bool graph = e < gh;
+      for (int mi = 0; mi < n_it; ++mi, ++it) {
+        const int s = it & 1;
+        const int m0 = (m_start + mi) * kBlockM;
+        const float* lv = vec + s * 256;
+        if (!mbar_wait(&bars[kAStFull], it & 1, abort_flag, 701) ||
+            !mbar_wait(&bars[kAPrep + s], (it >> 1) & 1, abort_flag, 702)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // valid query columns q in [q_lo, q_hi) for this key row
+        const int q_hi = kv_valid ? (si.len_q - m0) : 0;
+        const int q_lo = P.causal ? (kv_local - m0) : 0;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t sv[32], dp[32];
+          tmem_ld32(tS + lane_base + 32 * c, sv);
+          tmem_ld32(tDP + lane_base + 32 * c, dp);
+          tmem_ld_wait32(sv);
+          tmem_ld_wait32(dp);
+          uint32_t pp[16], dd[16];
+#pragma unroll
+          for (int k = 0; k < 32; k += 2) {
+            const int q0i = 32 * c + k;
+            const bool v0 = q0i >= q_lo && q0i < q_hi;
+            const bool v1 = q0i + 1 >= q_lo && q0i + 1 < q_hi;
+            const float p0 = v0 ? ex2(fmaf(__uint_as_float(sv[k]), sl2, -lv[q0i])) : 0.f;
+            const float p1 = v1 ? ex2(fmaf(__uint_as_float(sv[k + 1]), sl2, -lv[q0i + 1])) : 0.f;
+            const float d0 = p0 * (__uint_as_float(dp[k]) - lv[128 + q0i]);
+            const float d1 = p1 * (__uint_as_float(dp[k + 1]) - lv[128 + q0i + 1]);
+            pp[k >> 1] = pack_bf16(p0, p1);
+            dd[k >> 1] = pack_bf16(d0, d1);
+          }
+          tmem_st16(tS + lane_base + 16 * c, pp);
+          tmem_st16(tDP + lane_base + 16 * c, dd);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&bars[kAPReady]);
+        if (graph) {
+          if (!mbar_wait(&bars[kADrk], git & 1, abort_flag, 703)) {
+            ok = false;
+            break;
+          }
+          ++git;
+          tc_fence_after();
+          uint32_t rv[32];
+          if (RP == 16) {
+            tmem_ld16(tDRK + lane_base, rv);
+            tmem_ld_wait16(rv);
+          } else {
+            tmem_ld32(tDRK + lane_base, rv);
+            tmem_ld_wait32(rv);
+          }
+#pragma unroll
+          for (int i = 0; i < RP; ++i) drk_acc[i] += __uint_as_float(rv[i]);
+        }
+        tc_fence_before();
+        mbar_arrive(&bars[kATmemFree]);
+        if (graph && mi == n_it - 1) {
+          if (kv_valid) {
+            __nv_bfloat16* dst = p.drk + si.b * p.drk_sb + h * p.drk_sh + krow * p.drk_sr;
+#pragma unroll
+            for (int c = 0; c < RP; c += 8) {
+              if (c < P.rank) {
+                uint4 w;
+                uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                  wp[i] = pack_bf16(drk_acc[c + 2 * i] * scale, drk_acc[c + 2 * i + 1] * scale);
+                *reinterpret_cast<uint4*>(dst + c) = w;
+              }
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < RP; ++i) drk_acc[i] = 0.f;
+        }
+      }
+    }
+    if (ok && mbar_wait(&bars[kAAllDone], 0, abort_flag, 704)) {
+      tc_fence_after();
+      __nv_bfloat16* dvrow = p.dv + si.b * p.dv_sb + hk * p.dv_sh + krow * p.dv_sr;
+      __nv_bfloat16* dkrow = p.dk + si.b * p.dk_sb + hk * p.dk_sh + krow * p.dk_sr;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tDV + lane_base + 32 * c, v);
+        tmem_ld_wait32(v);
+        if (kv_valid) store_row32(dvrow + 32 * c, v, 1.f);
+        tmem_ld32(tDK + lane_base + 32 * c, v);
+        tmem_ld_wait32(v);
+        if (kv_valid) store_row32(dkrow + 32 * c, v, scale);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// dQ / dR_q / d_gs  (Q-stationary)
+// ---------------------------------------------------------------------------
+template <int D, int RP>
+struct DqSmem {
+  static constexpr int kTile = 128 * D * 2;
+  static constexpr int kR = 128 * RP * 2;
+  static constexpr int kChunk = 128 * 128;
+  static constexpr int align(int x) { return (x + 1023) & ~1023; }
+  static constexpr int oQ = 0;
+  static constexpr int oDo = align(oQ + kTile);
+  static constexpr int oRq = align(oDo + kTile);
+  static constexpr int oK0 = align(oRq + kR);
+  static constexpr int oK1 = align(oK0 + kTile);
+  static constexpr int oV0 = align(oK1 + kTile);
+  static constexpr int oV1 = align(oV0 + kTile);
+  static constexpr int oRk0 = align(oV1 + kTile);
+  static constexpr int oRk1 = align(oRk0 + kR);
+  static constexpr int oBar = align(oRk1 + kR);
+  static constexpr int kNumBars = 12;
+  static constexpr int oMisc = oBar + kNumBars * 8;
+  static constexpr int kTotal = oMisc + 16 + 1024;
+};
+
+enum DqBar {
+  kBQFull = 0,
+  kBRqReady = 1,
+  kBKvFull = 2,   // +stage
+  kBKvEmpty = 4,  // +stage
+  kBStFull = 6,
+  kBPReady = 7,
+  kBAllDone = 8,
+};
+
+template <int D, int RP>
+__global__ void __launch_bounds__(192, 1)
+    fna2_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDo,
+                       const __grid_constant__ CUtensorMap tmRq, const __grid_constant__ CUtensorMap tmRk,
+                       const BwdParams p) {
+  using L = DqSmem<D, RP>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::oBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::oMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::oMisc + 4);
+
+  const ProblemDev& P = p.prob;
+  const int m_blk = p.n_mblocks - 1 - static_cast<int>(blockIdx.x);
+  const int h = blockIdx.y;
+  const SeqInfo si = seq_info(P, blockIdx.z);
+  const int q0 = m_blk * kBlockM;
+  if (q0 >= si.len_q) return;
+  const int hk = h / (P.heads / P.heads_kv);
+  const bool graph = h < P.heads_graph;
+  const int kv_end = P.causal ? min(si.len_k, q0 + kBlockM) : si.len_k;
+  const int n_tiles = kv_end > 0 ? (kv_end + kBlockN - 1) / kBlockN : 0;
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int tid = threadIdx.x;
+  const float scale = P.scale;
+
+  if (n_tiles == 0) {
+    if (tid < kBlockM && q0 + tid < si.len_q) {
+      const int64_t row = si.q_start + q0 + tid;
+      zero_row(p.dq + si.b * p.dq_sb + h * p.dq_sh + row * p.dq_sr, D);
+      if (graph) zero_row(p.drq + si.b * p.drq_sb + h * p.drq_sh + row * p.drq_sr, P.rank);
+    }
+    return;
+  }
+
+  if (tid == 0) {
+    mbar_init(&bars[kBQFull], 1);
+    mbar_init(&bars[kBRqReady], 128);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars[kBKvFull + s], 1);
+      mbar_init(&bars[kBKvEmpty + s], 1);
+    }
+    mbar_init(&bars[kBStFull], 1);
+    mbar_init(&bars[kBPReady], 128);
+    mbar_init(&bars[kBAllDone], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tDQ = tmem + 0, tDRQ = tmem + 128, tS = tmem + 256, tDP = tmem + 384;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      const int qrow = si.q_start + q0;
+      mbar_expect_tx(&bars[kBQFull], 2 * L::kTile + (graph ? L::kR : 0));
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        tma_load_4d(smem + L::oQ + c * L::kChunk, &tmQ, &bars[kBQFull], c * 64, qrow, h, si.b);
+        tma_load_4d(smem + L::oDo + c * L::kChunk, &tmDo, &bars[kBQFull], c * 64, qrow, h, si.b);
+      }
+      if (graph) tma_load_4d(smem + L::oRq, &tmRq, &bars[kBQFull], 0, qrow, h, si.b);
+      for (int j = 0; j < n_tiles; ++j) {
+        const int s = j & 1;
+        if (j >= 2 && !mbar_wait(&bars[kBKvEmpty + s], ((j >> 1) - 1) & 1, abort_flag, 801)) break;
+        const int krow = si.k_start + j * kBlockN;
+        mbar_expect_tx(&bars[kBKvFull + s], 2 * L::kTile + (graph ? L::kR : 0));
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_4d(smem + (s ? L::oK1 : L::oK0) + c * L::kChunk, &tmK, &bars[kBKvFull + s], c * 64, krow, hk,
+                      si.b);
+          tma_load_4d(smem + (s ? L::oV1 : L::oV0) + c * L::kChunk, &tmV, &bars[kBKvFull + s], c * 64, krow, hk,
+                      si.b);
+        }
+        if (graph) tma_load_4d(smem + (s ? L::oRk1 : L::oRk0), &tmRk, &bars[kBKvFull + s], 0, krow, h, si.b);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t idesc_dq = make_idesc_bf16(128, D, 0, 1);
+      constexpr uint32_t idesc_drq = make_idesc_bf16(128, RP, 0, 1);
+      const uint32_t r_layout = r_layout_of(RP);
+      const uint32_t r_sbo = 8 * RP * 2;
+      const uint32_t sQ = smem_u32(smem + L::oQ), sDo = smem_u32(smem + L::oDo), sRq = smem_u32(smem + L::oRq);
+      bool ok = mbar_wait(&bars[kBQFull], 0, abort_flag, 901);
+      if (ok && graph) ok = mbar_wait(&bars[kBRqReady], 0, abort_flag, 902);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int s = j & 1;
+        const uint32_t sK = smem_u32(smem + (s ? L::oK1 : L::oK0));
+        const uint32_t sV = smem_u32(smem + (s ? L::oV1 : L::oV0));
+        const uint32_t sRk = smem_u32(smem + (s ? L::oRk1 : L::oRk0));
+        if (!mbar_wait(&bars[kBKvFull + s], (j >> 1) & 1, abort_flag, 903)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * L::kChunk + (kk & 3) * 32;
+          mma_ss(tS, make_sdesc(sQ + off, 16, 1024, kSwizzle128B), make_sdesc(sK + off, 16, 1024, kSwizzle128B),
+                 idesc_s, kk > 0);
+        }
+        if (graph) {
+#pragma unroll
+          for (int kk = 0; kk < RP / 16; ++kk)
+            mma_ss(tS, make_sdesc(sRq + kk * 32, 16, r_sbo, r_layout), make_sdesc(sRk + kk * 32, 16, r_sbo, r_layout),
+                   idesc_s, 1);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * L::kChunk + (kk & 3) * 32;
+          mma_ss(tDP, make_sdesc(sDo + off, 16, 1024, kSwizzle128B), make_sdesc(sV + off, 16, 1024, kSwizzle128B),
+                 idesc_s, kk > 0);
+        }
+        mma_commit(&bars[kBStFull]);
+        if (!mbar_wait(&bars[kBPReady], j & 1, abort_flag, 904)) break;
+        tc_fence_after();
+        // dQ += dS K ; dR_q += dS R_k  (dS in TMEM over the S columns)
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_ts(tDQ, tS + kk * 8, make_sdesc(sK + kk * 2048, L::kChunk, 1024, kSwizzle128B), idesc_dq,
+                 (j > 0 || kk > 0) ? 1u : 0u);
+        if (graph) {
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_ts(tDRQ, tS + kk * 8, make_sdesc(sRk + kk * 16 * RP * 2, 16, r_sbo, r_layout), idesc_drq,
+                   (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(&bars[kBKvEmpty + s]);
+        if (j == n_tiles - 1) mma_commit(&bars[kBAllDone]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax-gradient warps 0-3 (query rows)
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const int q_local = q0 + tid;
+    const bool row_ok = q_local < si.len_q;
+    const int64_t row = si.q_start + q_local;
+    const int64_t widx = (static_cast<int64_t>(si.b) * P.heads + h) * p.ws_sbh + row;
+    const float lse2 = row_ok ? p.ws_lse2[widx] : 0.f;
+    const float delta = row_ok ? p.ws_delta[widx] : 0.f;
+    const float sl2 = P.scale_log2;
+    const int limit = row_ok ? (P.causal ? min(si.len_k, q_local + 1) : si.len_k) : 0;
+    bool ok = true;
+    if (graph) {
+      ok = mbar_wait(&bars[kBQFull], 0, abort_flag, 1001);
+      if (ok) {
+        scale_rows_inplace<RP>(smem + L::oRq, tid, __ldg(P.gs + h) / scale);
+        fence_proxy_async_smem();
+      }
+      mbar_arrive(&bars[kBRqReady]);
+    }
+    for (int j = 0; ok && j < n_tiles; ++j) {
+      if (!mbar_wait(&bars[kBStFull], j & 1, abort_flag, 1002)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int nvalid = limit - j * kBlockN;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32], dp[32];
+        tmem_ld32(tS + lane_base + 32 * c, sv);
+        tmem_ld32(tDP + lane_base + 32 * c, dp);
+        tmem_ld_wait32(sv);
+        tmem_ld_wait32(dp);
+        uint32_t dd[16];
+#pragma unroll
+        for (int k = 0; k < 32; k += 2) {
+          const int kv = 32 * c + k;
+          const float p0 = kv < nvalid ? ex2(fmaf(__uint_as_float(sv[k]), sl2, -lse2)) : 0.f;
+          const float p1 = kv + 1 < nvalid ? ex2(fmaf(__uint_as_float(sv[k + 1]), sl2, -lse2)) : 0.f;
+          dd[k >> 1] = pack_bf16(p0 * (__uint_as_float(dp[k]) - delta), p1 * (__uint_as_float(dp[k + 1]) - delta));
+        }
+        tmem_st16(tS + lane_base + 16 * c, dd);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&bars[kBPReady]);
+    }
+    if (ok && mbar_wait(&bars[kBAllDone], 0, abort_flag, 1003)) {
+      tc_fence_after();
+      __nv_bfloat16* dqrow = p.dq + si.b * p.dq_sb + h * p.dq_sh + row * p.dq_sr;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tDQ + lane_base + 32 * c, v);
+        tmem_ld_wait32(v);
+        if (row_ok) store_row32(dqrow + 32 * c, v, scale);
+      }
+      if (graph) {
+        uint32_t rv[32];
+        if (RP == 16) {
+          tmem_ld16(tDRQ + lane_base, rv);
+          tmem_ld_wait16(rv);
+        } else {
+          tmem_ld32(tDRQ + lane_base, rv);
+          tmem_ld_wait32(rv);
+        }
+        float part = 0.f;
+        if (row_ok) {
+          const float gsh = __ldg(P.gs + h);
+          const __nv_bfloat16* rq = p.rq + si.b * p.rq_sb + h * p.rq_sh + row * p.rq_sr;
+          __nv_bfloat16* dst = p.drq + si.b * p.drq_sb + h * p.drq_sh + row * p.drq_sr;
+#pragma unroll
+          for (int c = 0; c < RP; c += 8) {
+            if (c >= P.rank) break;
+            const uint4 rw = *reinterpret_cast<const uint4*>(rq + c);
+            const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rw);
+            uint4 w;
+            uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float a0 = __uint_as_float(rv[c + 2 * i]), a1 = __uint_as_float(rv[c + 2 * i + 1]);
+              const float2 rr = __bfloat1622float2(r2[i]);
+              part = fmaf(rr.x, a0, part);
+              part = fmaf(rr.y, a1, part);
+              wp[i] = pack_bf16(a0 * gsh, a1 * gsh);
+            }
+            *reinterpret_cast<uint4*>(dst + c) = w;
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+        if (lane == 0) atomicAdd(p.dgs + h, part);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host-side launch (called from fna2_api.cu)
+// ---------------------------------------------------------------------------
+template <int D, int RP>
+cudaError_t launch_bwd_t(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, const CUtensorMap& dO,
+                         const CUtensorMap& rq, const CUtensorMap& rk, const BwdParams& p, cudaStream_t stream) {
+  const int bdim = p.prob.varlen ? 1 : p.batch;
+  {
+    const int rows = max(p.total_q_rows, p.total_k_rows);
+    dim3 grid((rows + 127) / 128, p.prob.heads, bdim);
+    fna2_bwd_pre_kernel<D><<<grid, 128, 0, stream>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  {
+    using L = DkdvSmem<D, RP>;
+    auto kern = fna2_bwd_dkdv_kernel<D, RP>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+    if (e != cudaSuccess) return e;
+    dim3 grid(p.n_nblocks, p.prob.heads_kv, p.batch);
+    kern<<<grid, 224, L::kTotal, stream>>>(q, k, v, dO, rq, rk, p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  {
+    using L = DqSmem<D, RP>;
+    auto kern = fna2_bwd_dq_kernel<D, RP>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+    if (e != cudaSuccess) return e;
+    dim3 grid(p.n_mblocks, p.prob.heads, p.batch);
+    kern<<<grid, 192, L::kTotal, stream>>>(q, k, v, dO, rq, rk, p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t launch_bwd(int D, int RP, const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
+                       const CUtensorMap& dO, const CUtensorMap& rq, const CUtensorMap& rk, const BwdParams& p,
+                       cudaStream_t stream) {
+  if (D == 64 && RP == 16) return launch_bwd_t<64, 16>(q, k, v, dO, rq, rk, p, stream);
+  if (D == 64 && RP == 32) return launch_bwd_t<64, 32>(q, k, v, dO, rq, rk, p, stream);
+  if (D == 128 && RP == 16) return launch_bwd_t<128, 16>(q, k, v, dO, rq, rk, p, stream);
+  if (D == 128 && RP == 32) return launch_bwd_t<128, 32>(q, k, v, dO, rq, rk, p, stream);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace fna2

@@ -1,0 +1,401 @@
+// FNA2 forward on sm_100a: O = softmax(scale*Q K^T + gs*R_q R_k^T [causal]) V
+// and LSE, dense [B,H,S,D] and varlen [T,H,D] through the same kernel.
+//
+// Reference semantics: FNA2/flash_naylis_attn.py:58-201 (dense) and :208-349
+// (varlen): bias only on graph heads h < H_G, GQA kv_head = h / (H/H_KV),
+// causal on sequence-local positions, O = acc/(l+1e-6), LSE = m + log(l+1e-6).
+//
+// Design (one CTA per 128-row query tile of one head and sequence):
+//   warps 0-3  softmax: thread t owns query row t = TMEM lane t.  Reads the
+//              128x128 fp32 score tile S from TMEM, applies masks, keeps the
+//              running max/sum in registers, writes P (bf16) back into the
+//              same TMEM columns, rescales O in TMEM only when the max grew
+//              by more than 2^8 (exactly compensated at the end).
+//   warp 4     TMA producer: Q and R_q once; K(+R_k) and V tiles through two
+//              separate 2-stage mbarrier rings (K runs one tile ahead of V).
+//   warp 5     allocates 512 TMEM columns; one thread issues tcgen05.mma:
+//                S_b  = Q K^T + R~_q R_k^T   (SS, K = D + r_pad; the bias is an
+//                       extra K slice of the same accumulation, with
+//                       R~_q = R_q * gs/scale staged in shared memory)
+//                O   += P V                  (TS, P read from TMEM)
+// TMEM columns: O [0,128), S_0 [128,256), S_1 [256,384).
+#include "fna2_kernels.cuh"
+#include "ptx.cuh"
+
+namespace fna2 {
+
+template <int D, int RP>
+struct FwdSmem {
+  static constexpr int kQBytes = kBlockM * D * 2;
+  static constexpr int kRqBytes = kBlockM * RP * 2;
+  static constexpr int kKBytes = kBlockN * D * 2;
+  static constexpr int kRkBytes = kBlockN * RP * 2;
+  static constexpr int kVBytes = kBlockN * D * 2;
+  static constexpr int kChunk = 128 * 128;  // one 64-column chunk of a 128-row tile (bytes)
+  static constexpr int align(int x) { return (x + 1023) & ~1023; }
+  static constexpr int oQ = 0;
+  static constexpr int oRq = align(oQ + kQBytes);
+  static constexpr int oK0 = align(oRq + kRqBytes);
+  static constexpr int oK1 = align(oK0 + kKBytes);
+  static constexpr int oRk0 = align(oK1 + kKBytes);
+  static constexpr int oRk1 = align(oRk0 + kRkBytes);
+  static constexpr int oV0 = align(oRk1 + kRkBytes);
+  static constexpr int oV1 = align(oV0 + kVBytes);
+  static constexpr int oBar = align(oV1 + kVBytes);
+  static constexpr int kNumBars = 16;
+  static constexpr int oMisc = oBar + kNumBars * 8;
+  static constexpr int kTotal = oMisc + 16 + 1024;  // + slack for runtime 1024 B alignment
+};
+
+enum FwdBar {
+  kBarQFull = 0,
+  kBarRqReady = 1,
+  kBarKFull = 2,    // +stage
+  kBarKEmpty = 4,   // +stage
+  kBarVFull = 6,    // +stage
+  kBarVEmpty = 8,   // +stage
+  kBarSFull = 10,   // +buffer
+  kBarPFull = 12,   // +buffer
+  kBarOReady = 14,
+};
+
+template <int D, int RP>
+__global__ void __launch_bounds__(192, 1)
+    fna2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmRq,
+                    const __grid_constant__ CUtensorMap tmRk, const FwdParams p) {
+  using L = FwdSmem<D, RP>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::oBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::oMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::oMisc + 4);
+
+  const ProblemDev& P = p.prob;
+  const int m_blk = p.n_mblocks - 1 - static_cast<int>(blockIdx.x);  // heaviest causal tiles first
+  const int h = blockIdx.y;
+  const SeqInfo si = seq_info(P, blockIdx.z);
+  const int q0 = m_blk * kBlockM;
+  if (q0 >= si.len_q) return;
+  const int hk = h / (P.heads / P.heads_kv);
+  const bool graph = h < P.heads_graph;
+  const int kv_end = P.causal ? min(si.len_k, q0 + kBlockM) : si.len_k;
+  const int n_tiles = kv_end > 0 ? (kv_end + kBlockN - 1) / kBlockN : 0;
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int tid = threadIdx.x;
+
+  if (n_tiles == 0) {
+    // No visible key: the reference's loop is empty, O = 0 and LSE = -inf.
+    if (tid < kBlockM && q0 + tid < si.len_q) {
+      const int row = si.q_start + q0 + tid;
+      __nv_bfloat16* orow = p.out + si.b * p.o_sb + h * p.o_sh + static_cast<int64_t>(row) * p.o_sr;
+      for (int c = 0; c < D; ++c) orow[c] = __float2bfloat16(0.f);
+      p.lse[(static_cast<int64_t>(si.b) * P.heads + h) * p.lse_sbh + row] = -INFINITY;
+    }
+    return;
+  }
+
+  if (tid == 0) {
+    mbar_init(&bars[kBarQFull], 1);
+    mbar_init(&bars[kBarRqReady], kBlockM);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars[kBarKFull + s], 1);
+      mbar_init(&bars[kBarKEmpty + s], 1);
+      mbar_init(&bars[kBarVFull + s], 1);
+      mbar_init(&bars[kBarVEmpty + s], 1);
+      mbar_init(&bars[kBarSFull + s], 1);
+      mbar_init(&bars[kBarPFull + s], kBlockM);
+    }
+    mbar_init(&bars[kBarOReady], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      if (graph) {
+        tma_prefetch_desc(&tmRq);
+        tma_prefetch_desc(&tmRk);
+      }
+      const int qrow = si.q_start + q0;
+      mbar_expect_tx(&bars[kBarQFull], L::kQBytes + (graph ? L::kRqBytes : 0));
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c)
+        tma_load_4d(smem + L::oQ + c * L::kChunk, &tmQ, &bars[kBarQFull], c * 64, qrow, h, si.b);
+      if (graph) tma_load_4d(smem + L::oRq, &tmRq, &bars[kBarQFull], 0, qrow, h, si.b);
+
+      auto load_k = [&](int j) -> bool {
+        const int s = j & 1;
+        if (j >= 2 && !mbar_wait(&bars[kBarKEmpty + s], ((j >> 1) - 1) & 1, abort_flag, 101)) return false;
+        uint8_t* dk = smem + (s ? L::oK1 : L::oK0);
+        const int krow = si.k_start + j * kBlockN;
+        mbar_expect_tx(&bars[kBarKFull + s], L::kKBytes + (graph ? L::kRkBytes : 0));
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_4d(dk + c * L::kChunk, &tmK, &bars[kBarKFull + s], c * 64, krow, hk, si.b);
+        if (graph) tma_load_4d(smem + (s ? L::oRk1 : L::oRk0), &tmRk, &bars[kBarKFull + s], 0, krow, h, si.b);
+        return true;
+      };
+      auto load_v = [&](int j) -> bool {
+        const int s = j & 1;
+        if (j >= 2 && !mbar_wait(&bars[kBarVEmpty + s], ((j >> 1) - 1) & 1, abort_flag, 102)) return false;
+        uint8_t* dv = smem + (s ? L::oV1 : L::oV0);
+        const int krow = si.k_start + j * kBlockN;
+        mbar_expect_tx(&bars[kBarVFull + s], L::kVBytes);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_4d(dv + c * L::kChunk, &tmV, &bars[kBarVFull + s], c * 64, krow, hk, si.b);
+        return true;
+      };
+      bool ok = load_k(0);
+      if (ok && n_tiles > 1) ok = load_k(1);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        ok = load_v(j);
+        if (ok && j + 2 < n_tiles) ok = load_k(j + 2);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(kBlockM, kBlockN, 0, 0);
+      constexpr uint32_t idesc_pv = make_idesc_bf16(kBlockM, D, 0, 1);
+      constexpr uint32_t r_layout = RP == 16 ? kSwizzle32B : (RP == 32 ? kSwizzle64B : kSwizzle128B);
+      constexpr uint32_t r_sbo = 8 * RP * 2;
+      const uint32_t sQ = smem_u32(smem + L::oQ);
+      const uint32_t sRq = smem_u32(smem + L::oRq);
+      const uint32_t tO = tmem;
+      bool ok = mbar_wait(&bars[kBarQFull], 0, abort_flag, 201);
+      if (ok && graph) ok = mbar_wait(&bars[kBarRqReady], 0, abort_flag, 202);
+      tc_fence_after();
+
+      auto issue_s = [&](int j) -> bool {
+        const int b = j & 1;
+        if (!mbar_wait(&bars[kBarKFull + b], (j >> 1) & 1, abort_flag, 203)) return false;
+        tc_fence_after();
+        const uint32_t sK = smem_u32(smem + (b ? L::oK1 : L::oK0));
+        const uint32_t tS = tmem + 128 + 128 * b;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * L::kChunk + (kk & 3) * 32;
+          mma_ss(tS, make_sdesc(sQ + off, 16, 1024, kSwizzle128B), make_sdesc(sK + off, 16, 1024, kSwizzle128B),
+                 idesc_s, kk > 0);
+        }
+        if (graph) {
+          const uint32_t sRk = smem_u32(smem + (b ? L::oRk1 : L::oRk0));
+#pragma unroll
+          for (int kk = 0; kk < RP / 16; ++kk)
+            mma_ss(tS, make_sdesc(sRq + kk * 32, 16, r_sbo, r_layout), make_sdesc(sRk + kk * 32, 16, r_sbo, r_layout),
+                   idesc_s, 1);
+        }
+        mma_commit(&bars[kBarKEmpty + b]);
+        mma_commit(&bars[kBarSFull + b]);
+        return true;
+      };
+
+      if (ok) ok = issue_s(0);
+      if (ok && n_tiles > 1) ok = issue_s(1);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int b = j & 1;
+        if (!mbar_wait(&bars[kBarPFull + b], (j >> 1) & 1, abort_flag, 204)) break;
+        if (!mbar_wait(&bars[kBarVFull + b], (j >> 1) & 1, abort_flag, 205)) break;
+        tc_fence_after();
+        const uint32_t sV = smem_u32(smem + (b ? L::oV1 : L::oV0));
+        const uint32_t tP = tmem + 128 + 128 * b;
+#pragma unroll
+        for (int kk = 0; kk < kBlockN / 16; ++kk)
+          mma_ts(tO, tP + kk * 8, make_sdesc(sV + kk * 2048, L::kChunk, 1024, kSwizzle128B), idesc_pv,
+                 (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&bars[kBarVEmpty + b]);
+        mma_commit(&bars[kBarOReady]);
+        if (j + 2 < n_tiles) ok = issue_s(j + 2);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax (warps 0-3)
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t tO = tmem + lane_base;
+    const int q_local = q0 + tid;
+    const float sl2 = P.scale_log2;
+    bool ok = true;
+
+    if (graph) {
+      // R~_q = R_q * gs/scale in place (element-wise, so independent of the swizzle).
+      ok = mbar_wait(&bars[kBarQFull], 0, abort_flag, 301);
+      if (ok) {
+        const float f = __ldg(P.gs + h) / P.scale;
+        uint4* rrow = reinterpret_cast<uint4*>(smem + L::oRq + tid * RP * 2);
+#pragma unroll
+        for (int u = 0; u < RP / 8; ++u) {
+          uint4 w = rrow[u];
+          uint32_t* e = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            __nv_bfloat162 v2 = *reinterpret_cast<__nv_bfloat162*>(&e[i]);
+            float2 f2 = __bfloat1622float2(v2);
+            e[i] = pack_bf16(f2.x * f, f2.y * f);
+          }
+          rrow[u] = w;
+        }
+        fence_proxy_async_smem();
+      }
+      mbar_arrive(&bars[kBarRqReady]);
+    }
+
+    const int limit = P.causal ? min(si.len_k, q_local + 1) : si.len_k;
+    float m_use = -INFINITY, m_true = -INFINITY, l = 0.f;
+    uint32_t r[128];
+    for (int j = 0; ok && j < n_tiles; ++j) {
+      const int b = j & 1;
+      const uint32_t tS = tmem + lane_base + 128 + 128 * b;
+      if (!mbar_wait(&bars[kBarSFull + b], (j >> 1) & 1, abort_flag, 302)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tS + 32 * c, r + 32 * c);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld_wait32(r + 32 * c);
+
+      const int nvalid = limit - j * kBlockN;
+      float mx = -INFINITY;
+      if (nvalid >= kBlockN) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) mx = fmaxf(mx, __uint_as_float(r[i]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) {
+          const float x = i < nvalid ? __uint_as_float(r[i]) : -INFINITY;
+          r[i] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
+        }
+      }
+      mx *= sl2;
+      m_true = fmaxf(m_true, mx);
+      float alpha = 1.f;
+      bool rescale = false;
+      if (m_true - m_use > 8.f || m_use == -INFINITY) {
+        // grow the reference max; O (if any) must be scaled by alpha
+        alpha = (m_use == -INFINITY) ? 0.f : ex2(m_use - m_true);
+        rescale = (j > 0);
+        m_use = m_true;
+      }
+      const float mb = (m_use == -INFINITY) ? 0.f : m_use;
+      float rs = 0.f;
+#pragma unroll
+      for (int i = 0; i < 128; i += 2) {
+        const float p0 = ex2(fmaf(__uint_as_float(r[i]), sl2, -mb));
+        const float p1 = ex2(fmaf(__uint_as_float(r[i + 1]), sl2, -mb));
+        rs += p0 + p1;
+        r[i >> 1] = pack_bf16(p0, p1);
+      }
+      l = l * alpha + rs;
+      // P (bf16 pairs) over the first 64 columns of this S buffer
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_st16(tS + 16 * c, r + 16 * c);
+
+      if (j > 0) {
+        // previous P V must be complete before O is touched (and before the
+        // next S buffer can be reused by the issuer, which orders it anyway)
+        if (!mbar_wait(&bars[kBarOReady], (j - 1) & 1, abort_flag, 303)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, rescale)) {
+          const float a = rescale ? alpha : 1.f;
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + 32 * c, o);
+            tmem_ld_wait32(o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * a);
+            tmem_st32(tO + 32 * c, o);
+          }
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&bars[kBarPFull + b]);
+    }
+
+    if (ok && mbar_wait(&bars[kBarOReady], (n_tiles - 1) & 1, abort_flag, 304)) {
+      tc_fence_after();
+      // exact reference normalisation with the true running max
+      const float corr = (m_use == -INFINITY) ? 0.f : ex2(m_use - m_true);
+      const float l_true = l * corr;
+      const float inv = corr / (l_true + kEps);
+      const bool row_ok = q_local < si.len_q;
+      const int row = si.q_start + q_local;
+      __nv_bfloat16* orow = p.out + si.b * p.o_sb + h * p.o_sh + static_cast<int64_t>(row) * p.o_sr;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + 32 * c, o);
+        tmem_ld_wait32(o);
+        if (row_ok) {
+          uint4 w[4];
+          uint32_t* wp = reinterpret_cast<uint32_t*>(w);
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            wp[i] = pack_bf16(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+          uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = w[i];
+        }
+      }
+      if (row_ok) {
+        const float lse = (m_true == -INFINITY) ? -INFINITY : (m_true + lg2(l_true + kEps)) * kLn2;
+        p.lse[(static_cast<int64_t>(si.b) * P.heads + h) * p.lse_sbh + row] = lse;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host-side launch helper (called from fna2_api.cu)
+// ---------------------------------------------------------------------------
+template <int D, int RP>
+cudaError_t launch_fwd_t(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, const CUtensorMap& rq,
+                         const CUtensorMap& rk, const FwdParams& p, int grid_y, int grid_z, cudaStream_t stream) {
+  using L = FwdSmem<D, RP>;
+  auto kern = fna2_fwd_kernel<D, RP>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
+  if (e != cudaSuccess) return e;
+  dim3 grid(p.n_mblocks, grid_y, grid_z);
+  kern<<<grid, 192, L::kTotal, stream>>>(q, k, v, rq, rk, p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fwd(int D, int RP, const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
+                       const CUtensorMap& rq, const CUtensorMap& rk, const FwdParams& p, int grid_y, int grid_z,
+                       cudaStream_t stream) {
+  if (D == 64 && RP == 16) return launch_fwd_t<64, 16>(q, k, v, rq, rk, p, grid_y, grid_z, stream);
+  if (D == 64 && RP == 32) return launch_fwd_t<64, 32>(q, k, v, rq, rk, p, grid_y, grid_z, stream);
+  if (D == 128 && RP == 16) return launch_fwd_t<128, 16>(q, k, v, rq, rk, p, grid_y, grid_z, stream);
+  if (D == 128 && RP == 32) return launch_fwd_t<128, 32>(q, k, v, rq, rk, p, grid_y, grid_z, stream);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace fna2

@@ -1,0 +1,94 @@
+// Device-side parameter blocks and shared constants of the FNA2 kernels.
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+
+namespace fna2 {
+
+constexpr int kBlockM = 128;  // query rows per tile (one TMEM lane / softmax thread per row)
+constexpr int kBlockN = 128;  // key rows per tile
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kEps = 1e-6f;  // O = acc/(l+1e-6), LSE = m + log(l+1e-6)  (flash_naylis_attn.py:192,195)
+
+// Sequence bounds of one (batch or packed sequence) index. Dense problems have
+// all sequences of length seqlen_q/seqlen_k starting at row 0 of their batch.
+struct SeqInfo {
+  int q_start, k_start;  // first row in the row dimension of the tensor maps
+  int len_q, len_k;      // sequence lengths
+  int b;                 // batch coordinate (0 for varlen)
+};
+
+struct ProblemDev {
+  int heads, heads_kv, heads_graph, head_dim, rank;
+  int seqlen_q, seqlen_k;  // dense lengths; varlen: max lengths (grid sizing only)
+  int varlen, causal;
+  const int* cu_q;
+  const int* cu_k;
+  float scale;       // softmax_scale
+  float scale_log2;  // softmax_scale * log2(e)
+  const float* gs;   // graph_scale [H_G]
+};
+
+__device__ __forceinline__ SeqInfo seq_info(const ProblemDev& p, int bz) {
+  SeqInfo s;
+  if (p.varlen) {
+    s.q_start = __ldg(p.cu_q + bz);
+    s.len_q = __ldg(p.cu_q + bz + 1) - s.q_start;
+    s.k_start = __ldg(p.cu_k + bz);
+    s.len_k = __ldg(p.cu_k + bz + 1) - s.k_start;
+    s.b = 0;
+  } else {
+    s.q_start = 0;
+    s.k_start = 0;
+    s.len_q = p.seqlen_q;
+    s.len_k = p.seqlen_k;
+    s.b = bz;
+  }
+  return s;
+}
+
+struct FwdParams {
+  ProblemDev prob;
+  __nv_bfloat16* out;
+  int64_t o_sb, o_sh, o_sr;  // element strides (batch, head, row); column stride is 1
+  float* lse;                // index (b*H + h) * lse_sbh + row
+  int64_t lse_sbh;
+  int n_mblocks;             // grid.x
+};
+
+struct BwdParams {
+  ProblemDev prob;
+  // forward output / upstream gradient, row-major bf16 with unit column stride
+  const __nv_bfloat16* out;
+  int64_t o_sb, o_sh, o_sr;
+  const __nv_bfloat16* dout;
+  int64_t do_sb, do_sh, do_sr;
+  const float* lse;  // forward LSE, index (b*H + h) * lse_sbh + row
+  int64_t lse_sbh;
+  // workspace: per (b*H + h) rows of log2-domain LSE and Delta = rowsum(dO*O)
+  float* ws_lse2;
+  float* ws_delta;
+  int64_t ws_sbh;  // rows per (b,h) slot in the workspace (>= rows of the q tensor)
+  // gradients
+  __nv_bfloat16* dq;
+  int64_t dq_sb, dq_sh, dq_sr;
+  __nv_bfloat16* dk;
+  int64_t dk_sb, dk_sh, dk_sr;
+  __nv_bfloat16* dv;
+  int64_t dv_sb, dv_sh, dv_sr;
+  __nv_bfloat16* drq;
+  int64_t drq_sb, drq_sh, drq_sr;
+  __nv_bfloat16* drk;
+  int64_t drk_sb, drk_sh, drk_sr;
+  const __nv_bfloat16* rq;  // raw R_q rows (for d_gs = sum R_q * dS R_k)
+  int64_t rq_sb, rq_sh, rq_sr;
+  float* dgs;               // [H_G], accumulated with atomics (zeroed by the pre kernel)
+  int total_q_rows;         // rows of q per (b,h) slot: dense S, varlen T
+  int total_k_rows;
+  int batch;                // dense B or varlen N
+  int n_mblocks, n_nblocks;
+};
+
+}  // namespace fna2

@@ -1,0 +1,128 @@
+/*
+ * fna2.h -- C ABI of the B200-native (sm_100a) FNA2 fused relational-bias
+ * attention library (libfna2_b200.so).
+ *
+ * Computes, per query head h, query row i and key row j of one sequence:
+ *   S[i,j] = softmax_scale * <Q[i],K[j]> + gs[h] * <R_q[i],R_k[j]>   (h <  H_G)
+ *   S[i,j] = softmax_scale * <Q[i],K[j]>                             (h >= H_G)
+ *   S[i,j] = -inf when causal and j > i (positions local to the sequence)
+ *   O = softmax(S) V,  O = acc/(l+1e-6),  LSE = m + log(l+1e-6)
+ * with GQA kv_head = h / (H/H_KV), and the backward producing dQ, dK, dV,
+ * dR_q, dR_k and d_graph_scale.
+ *
+ * The entry points replace the launchers of the reference Python/Triton
+ * implementation (myAiByMe/FNA2, file FNA2/flash_naylis_attn.py):
+ *   fna2_fwd  <- _fna2_forward        (flash_naylis_attn.py:700-753)
+ *                _fna2_forward_varlen (flash_naylis_attn.py:756-804)
+ *   fna2_bwd  <- _fna2_backward        (flash_naylis_attn.py:807-892)
+ *                _fna2_backward_varlen (flash_naylis_attn.py:1215-1300)
+ * The reference's public op flash_naylis_attn() (flash_naylis_attn.py:1380)
+ * and its autograd Function (:1307-1373) are mirrored in Python by
+ * fna2_b200/flash_naylis_attn.py on top of these calls.
+ *
+ * Conventions
+ *   - All tensor pointers are device pointers; q/k/v/out/dout/r_q/r_k and all
+ *     gradients except d_graph_scale are bf16; graph_scale, lse and
+ *     d_graph_scale are fp32; cu_seqlens are int32.
+ *   - Fna2Tensor.stride holds element strides for (batch, head, row, col).
+ *     Dense tensors are [B, heads, S, X]; packed (varlen) tensors are
+ *     [T, heads, X] and use stride[0] = 0 (ignored), stride[1] = head stride,
+ *     stride[2] = token stride.  The column stride must be 1; the other
+ *     strides and every base pointer must be 16-byte aligned (TMA rule).
+ *   - lse is fp32, contiguous: [B, H, S] for dense problems and [H, T_q] for
+ *     packed ones.
+ *   - Varlen problems are always causal (the reference's varlen kernel has no
+ *     is_causal argument, flash_naylis_attn.py:1327-1332).
+ *   - Work is enqueued on `stream` (a cudaStream_t, NULL = legacy default);
+ *     the calls never synchronise the host.
+ *   - Return value: 0 on success, FNA2_ERR_INVALID (-1) for bad arguments
+ *     (message in fna2_last_error()), FNA2_ERR_CUDA (-2) when a CUDA call
+ *     failed (message likewise), FNA2_ERR_WORKSPACE (-3) for a too small
+ *     workspace.
+ */
+#ifndef FNA2_B200_H_
+#define FNA2_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FNA2_ABI_VERSION 1
+
+#define FNA2_OK 0
+#define FNA2_ERR_INVALID (-1)
+#define FNA2_ERR_CUDA (-2)
+#define FNA2_ERR_WORKSPACE (-3)
+
+typedef struct Fna2Tensor {
+  void* ptr;         /* device pointer (NULL allowed only where noted) */
+  int64_t stride[4]; /* element strides: batch, head, row, col */
+} Fna2Tensor;
+
+typedef struct Fna2Problem {
+  int32_t batch;       /* dense: B.  varlen: number of packed sequences N */
+  int32_t seqlen_q;    /* dense: S.  varlen: max_seqlen_q (>= every q length) */
+  int32_t seqlen_k;    /* dense: S.  varlen: max_seqlen_k (>= every k length) */
+  int32_t total_q;     /* varlen: rows of the packed q tensor (T_q); dense: unused */
+  int32_t total_k;     /* varlen: rows of the packed k/v tensors (T_k); dense: unused */
+  int32_t heads;       /* H */
+  int32_t heads_kv;    /* H_KV, divides H */
+  int32_t heads_graph; /* H_G <= H: heads [0, H_G) carry the rank-r bias */
+  int32_t head_dim;    /* D: 64 or 128 */
+  int32_t rank;        /* r: multiple of 8, <= 32 (ignored when H_G == 0) */
+  float softmax_scale; /* the reference defaults it to 1/sqrt(D) (:1415-1416) */
+  int32_t causal;      /* dense only; varlen is always causal */
+  const int32_t* cu_seqlens_q; /* varlen: device [N+1] cumulative q lengths; dense: NULL */
+  const int32_t* cu_seqlens_k; /* varlen: device [N+1] cumulative k lengths; dense: NULL */
+} Fna2Problem;
+
+typedef struct Fna2FwdArgs {
+  Fna2Problem prob;
+  Fna2Tensor q, k, v;   /* [B,H,S,D] / [B,H_KV,S,D]  or  [T,H,D] / [T,H_KV,D] */
+  Fna2Tensor r_q, r_k;  /* [B,H_G,S,r] or [T,H_G,r] (ptr may be NULL if H_G == 0) */
+  const float* graph_scale; /* [H_G] */
+  Fna2Tensor out;       /* same shape as q */
+  float* lse;           /* [B,H,S] or [H,T_q] */
+} Fna2FwdArgs;
+
+typedef struct Fna2BwdArgs {
+  Fna2Problem prob;
+  Fna2Tensor q, k, v, r_q, r_k;
+  const float* graph_scale;
+  Fna2Tensor out, dout;      /* forward output and upstream gradient (shape of q) */
+  const float* lse;          /* as written by fna2_fwd */
+  Fna2Tensor dq, dk, dv, dr_q, dr_k; /* outputs, shapes of the inputs */
+  float* d_graph_scale;      /* [H_G] output (overwritten) */
+  void* workspace;           /* device scratch, >= fna2_bwd_workspace_size() bytes, 256-B aligned */
+  size_t workspace_bytes;
+} Fna2BwdArgs;
+
+/* Forward: writes out and lse.  Replaces _fna2_forward / _fna2_forward_varlen. */
+int fna2_fwd(const Fna2FwdArgs* args, void* stream);
+
+/* Bytes of device scratch fna2_bwd needs for this problem (0 if invalid). */
+size_t fna2_bwd_workspace_size(const Fna2Problem* prob);
+
+/* Backward: writes dq, dk, dv, dr_q, dr_k and d_graph_scale.
+ * Replaces _fna2_backward / _fna2_backward_varlen. */
+int fna2_bwd(const Fna2BwdArgs* args, void* stream);
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char* fna2_last_error(void);
+
+/* Device watchdog: returns the site code recorded by a kernel whose bounded
+ * mbarrier wait gave up (0 = none) and clears it when reset != 0.
+ * Synchronises the current device. */
+int fna2_device_status(int reset);
+
+/* FNA2_ABI_VERSION of the loaded library. */
+int fna2_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FNA2_B200_H_ */
