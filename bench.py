@@ -1,0 +1,375 @@
+#!/usr/bin/env python3
+"""Benchmark of the FNA2 hot path: varlen causal fwd+bwd TFLOP/s on B200.
+
+Default workload (the metric's 1/2/4/8-GPU case): 512 packed
+sequences with lengths log-uniform in [128, 16384] (seeded), H = 32 heads (all
+graph heads), head_dim 128, rank 16, bf16, causal, gs = 1.  At N GPUs the
+sequences are LPT-partitioned by FLOPs across ranks (whole sequences per rank,
+no collective on the data path): total work is fixed, so scaling is "strong".
+
+One step = forward + backward of every sequence a rank owns.  ``value`` is
+total algorithmic FLOPs of the whole batch / max-over-ranks step time (device
+resident inputs); ``e2e`` is the same metric through the public API
+(``flash_naylis_attn`` + ``backward``) with the step's inputs copied from
+pinned host memory and d_graph_scale read back every step.
+
+``--impl reference`` times the reference's eager path restated on the CPU
+(oracle/fna2_oracle.py: materialised bias + SDPA + autograd, fp32, all host
+threads) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from fna2_b200 import flops as FL  # noqa: E402
+from fna2_b200 import partition as PT  # noqa: E402
+
+METRIC = "fwd+bwd TFLOP/s (bf16, varlen causal, d=128, r=16)"
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+
+def workload(name: str):
+    if name == "cfg5":
+        return dict(name="cfg5", lengths=PT.loguniform_lengths(512, 128, 16384, seed=0), H=32, D=128, r=16,
+                    desc="BASELINE config 5: 512 packed seqs, L log-uniform [128,16384] (seed 0), H32 D128 r16, "
+                         "causal bf16, gs=1")
+    if name == "cfg3":
+        return dict(name="cfg3", lengths=PT.uniform_int_lengths(16, 64, 4096, seed=0), H=16, D=128, r=16,
+                    desc="BASELINE config 3: 16 packed seqs, L uniform-int [64,4096] (seed 0), H16 D128 r16")
+    if name == "cfg2":
+        return dict(name="cfg2", lengths=[2048] * 8, H=16, D=128, r=16,
+                    desc="BASELINE config 2 as 8 packed sequences of 2048: H16 D128 r16")
+    if name == "cfg4":
+        return dict(name="cfg4", lengths=[32768], H=32, D=128, r=32,
+                    desc="BASELINE config 4: one sequence of 32768, H32 D128 r32")
+    raise ValueError(name)
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        load = [s for s in sm if s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(load), "sm_max_mhz": mx, "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's eager path (restated) on the host cores
+# ---------------------------------------------------------------------------
+
+def cpu_sample(w, budget_s: float, max_len: int = 2048):
+    """Time the fp32 eager oracle (fwd + autograd bwd) on whole sequences of the
+    workload (those with L <= max_len, in order) until ``budget_s`` is spent."""
+    from oracle import fna2_oracle as O
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    H, D, r = w["H"], w["D"], w["r"]
+    scale = 1.0 / math.sqrt(D)
+
+    def one(L, seed):
+        q, k, v, rq, rk, gs, do = O.make_dense_inputs(1, H, L, D, r, seed=seed)
+        ts = [t.requires_grad_(True) for t in (q, k, v, rq, rk, gs)]
+        out = O.sdpa_reference(*ts, scale, True)
+        out.backward(do)
+
+    one(128, 0)  # warm-up
+    done, flops, t0 = [], 0.0, time.perf_counter()
+    for i, L in enumerate(w["lengths"]):
+        if L > max_len:
+            continue
+        one(L, i)
+        done.append(L)
+        flops += FL.total_flops([L], H, H, D, r)
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{len(done)} whole sequences of the workload with L<=2048 (sum L={sum(done)}), "
+                      f"fp32 eager fwd+bwd (materialised bias + SDPA + autograd), {dt:.1f} s"}
+
+
+def run_reference(args, w):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    budget = 4.0
+    vals = []
+    for _ in range(args.warmup):
+        cpu_sample(w, 1.0)
+    for _ in range(args.steps):
+        vals.append(cpu_sample(w, budget))
+    v = statistics.median([x["value"] for x in vals])
+    last = vals[-1]
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": w["desc"], "sample": last["sample"]},
+        "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": last["cores"], "kind": "port",
+                         "sample": last["sample"]},
+        "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def run_gpu(args, w):
+    import torch.distributed as dist
+    from fna2_b200 import flash_naylis_attn
+    from fna2_b200.flash_naylis_attn import _fna2_backward, _fna2_forward
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    H, D, r = w["H"], w["D"], w["r"]
+    lengths = w["lengths"]
+    parts = PT.lpt_partition(lengths, world)
+    mine = [lengths[i] for i in parts[rank]]
+    cu = PT.cu_seqlens(mine)
+    T = cu[-1]
+    flops_all = FL.total_flops(lengths, H, H, D, r)
+    flops_mine = FL.total_flops(mine, H, H, D, r)
+    scale = 1.0 / math.sqrt(D)
+
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    def rnd(*shape, s=1.0):
+        return (torch.randn(*shape, device=dev, generator=g, dtype=torch.float32) * s).to(torch.bfloat16)
+    q, k, v = rnd(T, H, D), rnd(T, H, D), rnd(T, H, D)
+    rq, rk = rnd(T, H, r, s=r ** -0.5), rnd(T, H, r, s=r ** -0.5)
+    do = rnd(T, H, D)
+    gs = torch.ones(H, device=dev, dtype=torch.float32)
+    cu_t = torch.tensor(cu, dtype=torch.int32, device=dev)
+    msl = max(mine)
+    stream = torch.cuda.current_stream()
+
+    def mk_events(n):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+        for e in evs:
+            e.record(stream)
+        return evs
+
+    def step(evf=None, evb=None):
+        out, lse = _fna2_forward(q, k, v, rq, rk, gs, scale, True, cu_t, cu_t, msl, msl, launch_events=evf)
+        _fna2_backward(do, q, k, v, rq, rk, gs, out, lse, scale, True, cu_t, cu_t, msl, msl, launch_events=evb)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    K, W = args.steps, args.warmup
+    for _ in range(W):
+        step()
+    ev_f = [mk_events(2) for _ in range(K)]
+    ev_b = [mk_events(4) for _ in range(K)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    t0.record(stream)
+    for i in range(K):
+        step(ev_f[i], ev_b[i])
+    t1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    barrier()
+    ms = t0.elapsed_time(t1) / K
+    ms_t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    value = flops_all / (ms_max / 1e3) / 1e12
+
+    kern = {
+        "fwd": statistics.mean(ev_f[i][0].elapsed_time(ev_f[i][1]) for i in range(K)),
+        "bwd_pre": statistics.mean(ev_b[i][0].elapsed_time(ev_b[i][1]) for i in range(K)),
+        "bwd_dkdv": statistics.mean(ev_b[i][1].elapsed_time(ev_b[i][2]) for i in range(K)),
+        "bwd_dq": statistics.mean(ev_b[i][2].elapsed_time(ev_b[i][3]) for i in range(K)),
+    }
+    algo = {
+        "fwd": FL.fwd_flops(mine, H, H, D, r),
+        "bwd_dkdv": FL.dkdv_flops(mine, H, H, D, r),
+        "bwd_dq": FL.dq_flops(mine, H, H, D, r),
+    }
+    dom = max(algo, key=lambda n: kern[n])
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    peak = peaks.get("bf16_tflops_sustained")
+    peak_src = "measured sustained"
+    if peak is None:
+        peak, peak_src = 1400.0, "fallback sustained"
+    achieved = algo[dom] / (kern[dom] / 1e3) / 1e12
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
+            tr = json.load(f)
+        per_tok = tr.get(w["name"], {}).get(dom)
+        if per_tok is not None:
+            traffic = per_tok * T
+    except Exception:
+        pass
+
+    # ---------------- e2e through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        del ev_f, ev_b
+        torch.cuda.synchronize()
+        host = [t.to("cpu").pin_memory() for t in (q, k, v, rq, rk, do)]
+        h2d = sum(t.numel() * t.element_size() for t in host)
+        leaves = [q, k, v, rq, rk]   # device buffers the host inputs are copied into each step
+        dev_do = do
+        gsl = gs.clone().requires_grad_(True)
+        res_host = torch.empty(H, dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            for dst, src in zip(leaves + [dev_do], host):
+                dst.copy_(src, non_blocking=True)
+            ins = [t.detach().requires_grad_(True) for t in leaves]
+            gsl.grad = None
+            out = flash_naylis_attn(*ins, gsl, softmax_scale=scale, is_causal=True, cu_seqlens_q=cu_t,
+                                    cu_seqlens_k=cu_t, max_seqlen_q=msl, max_seqlen_k=msl)
+            out.backward(dev_do)
+            res_host.copy_(gsl.grad, non_blocking=True)
+            return ins, out
+
+        for _ in range(W):
+            e2e_step()
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(K):
+            keep = e2e_step()
+            del keep
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ems = torch.tensor([e0.elapsed_time(e1) / K], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(ems, op=dist.ReduceOp.MAX)
+        e2e = {"value": flops_all / (float(ems.item()) / 1e3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": res_host.numel() * 4 * world,
+               "ms_per_step": float(ems.item())}
+
+    from fna2_b200 import _lib
+    status = _lib.load().fna2_device_status(0)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_sample(w, args.cpu_budget)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": w["desc"], "total_tokens": sum(lengths), "sequences": len(lengths),
+                       "parallelism": f"sequence-sharded LPT x{world} (no data-path collective)",
+                       "l2": "inputs larger than L2 (no flush needed)" if sum(lengths) * H * D * 2 > 126e6
+                       else "inputs smaller than L2: not flushed"},
+            "roofline": {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": peak,
+                         "peak_source": peak_src, "unit": "TFLOP/s", "frac": achieved / peak,
+                         "traffic": traffic},
+            "kernels_ms": kern,
+            "e2e": e2e,
+            "gpu_launches": 4 * K,
+            "clocks": clk,
+            "cpu_baseline": cpu,
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="fna2", choices=["fna2", "reference"])
+    ap.add_argument("--workload", default="cfg5", choices=["cfg5", "cfg3", "cfg2", "cfg4"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    args = ap.parse_args()
+    w = workload(args.workload)
+    if args.impl == "reference":
+        run_reference(args, w)
+    else:
+        run_gpu(args, w)
+
+
+if __name__ == "__main__":
+    main()

@@ -56,6 +56,7 @@ class Fna2FwdArgs(ctypes.Structure):
         ("graph_scale", ctypes.c_void_p),
         ("out", Fna2Tensor),
         ("lse", ctypes.c_void_p),
+        ("launch_events", ctypes.c_void_p),
     ]
 
 
@@ -79,6 +80,7 @@ class Fna2BwdArgs(ctypes.Structure):
         ("d_graph_scale", ctypes.c_void_p),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
+        ("launch_events", ctypes.c_void_p),
     ]
 
 

@@ -229,7 +229,11 @@ extern "C" int fna2_fwd(const Fna2FwdArgs* a, void* stream) {
   p.lse = a->lse;
   p.lse_sbh = s.rows_q();
   p.n_mblocks = (s.Sq + kBlockM - 1) / kBlockM;
-  FNA2_CUDA(launch_fwd(s.D, s.RP, tq, tk, tv, trq, trk, p, s.H, s.B, static_cast<cudaStream_t>(stream)));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaEvent_t* ev = reinterpret_cast<cudaEvent_t*>(a->launch_events);
+  if (ev) FNA2_CUDA(cudaEventRecord(ev[0], st));
+  FNA2_CUDA(launch_fwd(s.D, s.RP, tq, tk, tv, trq, trk, p, s.H, s.B, st));
+  if (ev) FNA2_CUDA(cudaEventRecord(ev[1], st));
   return FNA2_OK;
 }
 
@@ -311,6 +315,7 @@ extern "C" int fna2_bwd(const Fna2BwdArgs* a, void* stream) {
   p.n_mblocks = (s.Sq + kBlockM - 1) / kBlockM;
   p.n_nblocks = (s.Sk + kBlockN - 1) / kBlockN;
   bwd_set_workspace(&p, a->workspace, s.batch_dim(), s.H, s.rows_q());
-  FNA2_CUDA(launch_bwd(s.D, s.RP, tq, tk, tv, tdo, trq, trk, p, static_cast<cudaStream_t>(stream)));
+  FNA2_CUDA(launch_bwd(s.D, s.RP, tq, tk, tv, tdo, trq, trk, p, static_cast<cudaStream_t>(stream),
+                       reinterpret_cast<cudaEvent_t*>(a->launch_events)));
   return FNA2_OK;
 }

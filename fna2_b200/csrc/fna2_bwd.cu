@@ -793,13 +793,19 @@ __global__ void __launch_bounds__(192, 1)
 // ---------------------------------------------------------------------------
 template <int D, int RP>
 cudaError_t launch_bwd_t(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, const CUtensorMap& dO,
-                         const CUtensorMap& rq, const CUtensorMap& rk, const BwdParams& p, cudaStream_t stream) {
+                         const CUtensorMap& rq, const CUtensorMap& rk, const BwdParams& p, cudaStream_t stream,
+                         cudaEvent_t* ev) {
   const int bdim = p.prob.varlen ? 1 : p.batch;
+  if (ev) {
+    cudaError_t e = cudaEventRecord(ev[0], stream);
+    if (e != cudaSuccess) return e;
+  }
   {
     const int rows = max(p.total_q_rows, p.total_k_rows);
     dim3 grid((rows + 127) / 128, p.prob.heads, bdim);
     fna2_bwd_pre_kernel<D><<<grid, 128, 0, stream>>>(p);
     cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess && ev) e = cudaEventRecord(ev[1], stream);
     if (e != cudaSuccess) return e;
   }
   {
@@ -810,6 +816,7 @@ cudaError_t launch_bwd_t(const CUtensorMap& q, const CUtensorMap& k, const CUten
     dim3 grid(p.n_nblocks, p.prob.heads_kv, p.batch);
     kern<<<grid, 224, L::kTotal, stream>>>(q, k, v, dO, rq, rk, p);
     e = cudaGetLastError();
+    if (e == cudaSuccess && ev) e = cudaEventRecord(ev[2], stream);
     if (e != cudaSuccess) return e;
   }
   {
@@ -820,6 +827,7 @@ cudaError_t launch_bwd_t(const CUtensorMap& q, const CUtensorMap& k, const CUten
     dim3 grid(p.n_mblocks, p.prob.heads, p.batch);
     kern<<<grid, 192, L::kTotal, stream>>>(q, k, v, dO, rq, rk, p);
     e = cudaGetLastError();
+    if (e == cudaSuccess && ev) e = cudaEventRecord(ev[3], stream);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -827,11 +835,11 @@ cudaError_t launch_bwd_t(const CUtensorMap& q, const CUtensorMap& k, const CUten
 
 cudaError_t launch_bwd(int D, int RP, const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
                        const CUtensorMap& dO, const CUtensorMap& rq, const CUtensorMap& rk, const BwdParams& p,
-                       cudaStream_t stream) {
-  if (D == 64 && RP == 16) return launch_bwd_t<64, 16>(q, k, v, dO, rq, rk, p, stream);
-  if (D == 64 && RP == 32) return launch_bwd_t<64, 32>(q, k, v, dO, rq, rk, p, stream);
-  if (D == 128 && RP == 16) return launch_bwd_t<128, 16>(q, k, v, dO, rq, rk, p, stream);
-  if (D == 128 && RP == 32) return launch_bwd_t<128, 32>(q, k, v, dO, rq, rk, p, stream);
+                       cudaStream_t stream, cudaEvent_t* ev) {
+  if (D == 64 && RP == 16) return launch_bwd_t<64, 16>(q, k, v, dO, rq, rk, p, stream, ev);
+  if (D == 64 && RP == 32) return launch_bwd_t<64, 32>(q, k, v, dO, rq, rk, p, stream, ev);
+  if (D == 128 && RP == 16) return launch_bwd_t<128, 16>(q, k, v, dO, rq, rk, p, stream, ev);
+  if (D == 128 && RP == 32) return launch_bwd_t<128, 32>(q, k, v, dO, rq, rk, p, stream, ev);
   return cudaErrorInvalidValue;
 }
 

@@ -133,8 +133,16 @@ def _validate(q, k, v, r_q, r_k, graph_scale, cu_q, cu_k):
 # launchers (the C-ABI calls)
 # ---------------------------------------------------------------------------
 
-def _fna2_forward(q, k, v, r_q, r_k, gs, softmax_scale, is_causal, cu_q=None, cu_k=None, max_q=0, max_k=0
-                  ) -> Tuple[torch.Tensor, torch.Tensor]:
+def _events_arg(events):
+    """ctypes array of raw cudaEvent_t handles (torch.cuda.Event, already created)."""
+    if not events:
+        return None, None
+    arr = (ctypes.c_void_p * len(events))(*[e.cuda_event for e in events])
+    return ctypes.cast(arr, ctypes.c_void_p), arr
+
+
+def _fna2_forward(q, k, v, r_q, r_k, gs, softmax_scale, is_causal, cu_q=None, cu_k=None, max_q=0, max_k=0,
+                  launch_events=None) -> Tuple[torch.Tensor, torch.Tensor]:
     """Forward launcher; replaces _fna2_forward / _fna2_forward_varlen
     (flash_naylis_attn.py:700-804).  Returns (out, lse); lse is [B,H,S] dense
     or [H,T] packed (fp32)."""
@@ -154,12 +162,13 @@ def _fna2_forward(q, k, v, r_q, r_k, gs, softmax_scale, is_causal, cu_q=None, cu
     a.graph_scale = gs.data_ptr() if gs.numel() else None
     a.out = _desc(out, varlen)
     a.lse = lse.data_ptr()
+    a.launch_events, keep = _events_arg(launch_events)
     _lib.check(lib.fna2_fwd(ctypes.byref(a), _stream()), "fna2_fwd")
     return out, lse
 
 
 def _fna2_backward(dout, q, k, v, r_q, r_k, gs, out, lse, softmax_scale, is_causal, cu_q=None, cu_k=None,
-                   max_q=0, max_k=0):
+                   max_q=0, max_k=0, launch_events=None):
     """Backward launcher; replaces _fna2_backward / _fna2_backward_varlen
     (flash_naylis_attn.py:807-892, :1215-1300).  Returns
     (dq, dk, dv, dr_q, dr_k, d_gs)."""
@@ -184,6 +193,7 @@ def _fna2_backward(dout, q, k, v, r_q, r_k, gs, out, lse, softmax_scale, is_caus
     a.d_graph_scale = d_gs.data_ptr() if hg else None
     a.workspace = ws.data_ptr()
     a.workspace_bytes = ws.numel()
+    a.launch_events, keep = _events_arg(launch_events)
     _lib.check(lib.fna2_bwd(ctypes.byref(a), _stream()), "fna2_bwd")
     return dq, dk, dv, dr_q, dr_k, d_gs
 

@@ -1,0 +1,54 @@
+"""FLOP-balanced partition of packed sequences across ranks (multi-GPU bench).
+
+Units are whole sequences (all heads of a sequence stay on one rank, so GQA
+groups never split and dK/dV need no cross-GPU reduction).  A unit's cost is
+its causal fwd+bwd FLOPs, proportional to L^2.  Longest-processing-time
+greedy: sort by cost descending, give each unit to the least loaded rank.
+"""
+from __future__ import annotations
+
+import heapq
+import math
+import random
+from typing import List, Sequence
+
+
+def lpt_partition(lengths: Sequence[int], world: int) -> List[List[int]]:
+    """Return, per rank, the sorted indices of the sequences it owns."""
+    if world < 1:
+        raise ValueError("world must be >= 1")
+    heap = [(0.0, r) for r in range(world)]
+    heapq.heapify(heap)
+    parts: List[List[int]] = [[] for _ in range(world)]
+    order = sorted(range(len(lengths)), key=lambda i: (-int(lengths[i]) ** 2, i))
+    for i in order:
+        load, r = heapq.heappop(heap)
+        parts[r].append(i)
+        heapq.heappush(heap, (load + float(lengths[i]) ** 2, r))
+    return [sorted(p) for p in parts]
+
+
+def imbalance(lengths: Sequence[int], parts: List[List[int]]) -> float:
+    """max rank cost / mean rank cost (1.0 = perfect)."""
+    costs = [sum(float(lengths[i]) ** 2 for i in p) for p in parts]
+    mean = sum(costs) / len(costs)
+    return max(costs) / mean if mean > 0 else 1.0
+
+
+def loguniform_lengths(n: int, lo: int, hi: int, seed: int = 0) -> List[int]:
+    """n lengths log-uniform in [lo, hi] (fp64 draws, rounded)."""
+    rng = random.Random(seed)
+    return [int(round(math.exp(rng.uniform(math.log(lo), math.log(hi))))) for _ in range(n)]
+
+
+def uniform_int_lengths(n: int, lo: int, hi: int, seed: int = 0) -> List[int]:
+    """n lengths uniform-int in [lo, hi]."""
+    rng = random.Random(seed)
+    return [rng.randint(lo, hi) for _ in range(n)]
+
+
+def cu_seqlens(lengths: Sequence[int]) -> List[int]:
+    cu = [0]
+    for L in lengths:
+        cu.append(cu[-1] + int(L))
+    return cu

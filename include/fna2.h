@@ -86,6 +86,8 @@ typedef struct Fna2FwdArgs {
   const float* graph_scale; /* [H_G] */
   Fna2Tensor out;       /* same shape as q */
   float* lse;           /* [B,H,S] or [H,T_q] */
+  void** launch_events; /* optional (NULL = off): 2 cudaEvent_t recorded on `stream`
+                           before and after the forward kernel, for per-kernel timing */
 } Fna2FwdArgs;
 
 typedef struct Fna2BwdArgs {
@@ -98,6 +100,8 @@ typedef struct Fna2BwdArgs {
   float* d_graph_scale;      /* [H_G] output (overwritten) */
   void* workspace;           /* device scratch, >= fna2_bwd_workspace_size() bytes, 256-B aligned */
   size_t workspace_bytes;
+  void** launch_events;      /* optional (NULL = off): 4 cudaEvent_t recorded on `stream` before the
+                                pre-pass, after it, after the dK/dV kernel and after the dQ kernel */
 } Fna2BwdArgs;
 
 /* Forward: writes out and lse.  Replaces _fna2_forward / _fna2_forward_varlen. */
