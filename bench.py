@@ -284,7 +284,11 @@ def run_gpu(args, w):
     if not args.no_e2e:
         del ev_f, ev_b
         torch.cuda.synchronize()
-        host = [t.to("cpu").pin_memory() for t in (q, k, v, rq, rk, do)]
+        host = []
+        for t in (q, k, v, rq, rk, do):  # pinned host copies, filled without a pageable intermediate
+            h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+            h.copy_(t)
+            host.append(h)
         h2d = sum(t.numel() * t.element_size() for t in host)
         leaves = [q, k, v, rq, rk]   # device buffers the host inputs are copied into each step
         dev_do = do

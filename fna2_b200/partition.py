@@ -52,3 +52,32 @@ def cu_seqlens(lengths: Sequence[int]) -> List[int]:
     for L in lengths:
         cu.append(cu[-1] + int(L))
     return cu
+
+
+def shard_token_index(lengths: Sequence[int], part: Sequence[int]) -> List[int]:
+    """Rows of the global packed tensor (sequences in index order) that the
+    sequences in ``part`` occupy, in the rank-local packing order."""
+    cu = cu_seqlens(lengths)
+    rows: List[int] = []
+    for i in part:
+        rows.extend(range(cu[i], cu[i + 1]))
+    return rows
+
+
+def scatter_rows(t, lengths: Sequence[int], parts: List[List[int]], rank: int):
+    """Rank-local packed slice of a global packed tensor [T, ...]."""
+    import torch
+    idx = torch.tensor(shard_token_index(lengths, parts[rank]), dtype=torch.long, device=t.device)
+    return t.index_select(0, idx)
+
+
+def gather_rows(local_tensors, lengths: Sequence[int], parts: List[List[int]]):
+    """Inverse of scatter_rows: place every rank's rows back in global order."""
+    import torch
+    T = sum(int(L) for L in lengths)
+    first = local_tensors[0]
+    out = first.new_zeros((T,) + tuple(first.shape[1:]))
+    for rank, t in enumerate(local_tensors):
+        idx = torch.tensor(shard_token_index(lengths, parts[rank]), dtype=torch.long, device=t.device)
+        out.index_copy_(0, idx, t)
+    return out

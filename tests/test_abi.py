@@ -1,0 +1,119 @@
+"""CPU tests of the C ABI: the library loads, exports every symbol include/fna2.h
+declares, the ctypes structs match the C layout, and invalid arguments are
+rejected on the host (no GPU needed: validation precedes any CUDA call)."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from fna2_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "fna2.h")
+
+
+def _declared():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(fna2_\w+)\s*\(", text, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    declared = _declared()
+    assert declared, "no declarations parsed"
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True).stdout
+    exported = set(re.findall(r"\sT\s(fna2_\w+)", out))
+    for name in declared:
+        assert name in exported, name
+        assert hasattr(lib, name)
+    assert set(_lib.EXPORTED) <= set(declared)
+
+
+def test_struct_layout_matches_c(tmp_path):
+    src = tmp_path / "sz.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "fna2.h"\n'
+                   'int main(){printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(Fna2Tensor), sizeof(Fna2Problem),'
+                   ' sizeof(Fna2FwdArgs), sizeof(Fna2BwdArgs), offsetof(Fna2BwdArgs, workspace_bytes),'
+                   ' offsetof(Fna2FwdArgs, launch_events));}\n')
+    exe = tmp_path / "sz"
+    subprocess.check_call(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)])
+    got = [int(x) for x in subprocess.check_output([str(exe)]).split()]
+    want = [ctypes.sizeof(_lib.Fna2Tensor), ctypes.sizeof(_lib.Fna2Problem), ctypes.sizeof(_lib.Fna2FwdArgs),
+            ctypes.sizeof(_lib.Fna2BwdArgs), _lib.Fna2BwdArgs.workspace_bytes.offset,
+            _lib.Fna2FwdArgs.launch_events.offset]
+    assert got == want
+
+
+def _fwd_args(**over):
+    a = _lib.Fna2FwdArgs()
+    p = a.prob
+    p.batch, p.seqlen_q, p.seqlen_k = 1, 128, 128
+    p.heads, p.heads_kv, p.heads_graph, p.head_dim, p.rank = 2, 2, 2, 128, 16
+    p.softmax_scale, p.causal = 0.088, 1
+    for k, v in over.items():
+        setattr(p, k, v)
+    return a
+
+
+@pytest.mark.parametrize("field,value,msg", [
+    ("head_dim", 96, "head_dim"),
+    ("heads_kv", 3, "heads_kv"),
+    ("heads_graph", 5, "heads_graph"),
+    ("rank", 12, "rank"),
+    ("softmax_scale", 0.0, "softmax_scale"),
+])
+def test_invalid_problem_rejected_on_host(field, value, msg):
+    lib = _lib.load()
+    a = _fwd_args(**{field: value})
+    rc = lib.fna2_fwd(ctypes.byref(a), None)
+    assert rc == _lib.FNA2_ERR_INVALID
+    assert msg in lib.fna2_last_error().decode()
+
+
+def test_null_and_misaligned_tensors_rejected():
+    lib = _lib.load()
+    a = _fwd_args()
+    rc = lib.fna2_fwd(ctypes.byref(a), None)  # q.ptr is NULL
+    assert rc == _lib.FNA2_ERR_INVALID and "q: null pointer" in lib.fna2_last_error().decode()
+    a.q.ptr = 0x1008  # not 16-byte aligned
+    a.q.stride[:] = (256 * 128, 128 * 128, 128, 1)
+    rc = lib.fna2_fwd(ctypes.byref(a), None)
+    assert rc == _lib.FNA2_ERR_INVALID and "16-byte" in lib.fna2_last_error().decode()
+    a.q.ptr = 0x1000
+    a.q.stride[:] = (256 * 128, 128 * 128, 128, 2)
+    rc = lib.fna2_fwd(ctypes.byref(a), None)
+    assert rc == _lib.FNA2_ERR_INVALID and "column stride" in lib.fna2_last_error().decode()
+
+
+def test_empty_problem_is_a_no_op():
+    lib = _lib.load()
+    a = _fwd_args(batch=0)
+    assert lib.fna2_fwd(ctypes.byref(a), None) == _lib.FNA2_OK
+
+
+def test_workspace_size():
+    lib = _lib.load()
+    a = _fwd_args()
+    n = lib.fna2_bwd_workspace_size(ctypes.byref(a.prob))
+    assert n >= 2 * 1 * 2 * 128 * 4 and n % 256 == 0
+    bad = _fwd_args(head_dim=80)
+    assert lib.fna2_bwd_workspace_size(ctypes.byref(bad.prob)) == 0
+
+
+def test_python_entry_refuses_cpu_tensors():
+    import torch
+    from fna2_b200 import flash_naylis_attn
+    q = torch.zeros(1, 2, 8, 64, dtype=torch.bfloat16)
+    r = torch.zeros(1, 2, 8, 16, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        flash_naylis_attn(q, q, q, r, r, torch.ones(2))
+    with pytest.raises(AssertionError):
+        flash_naylis_attn(q, q, q, r.float(), r, torch.ones(2))
+
+
+def test_module_constants_keep_reference_contract():
+    import fna2_b200
+    assert fna2_b200.BLOCK_R == 32  # NaylisAttention requires rel_rank == BLOCK_R (attention_fna2.py:225)
+    assert fna2_b200.BLOCK_M == 128
