@@ -19,7 +19,8 @@ FNA2_ERR_CUDA = -2
 FNA2_ERR_WORKSPACE = -3
 
 EXPORTED = ["fna2_fwd", "fna2_bwd", "fna2_bwd_workspace_size", "fna2_last_error", "fna2_device_status",
-            "fna2_abi_version"]
+            "fna2_abi_version", "fna2_bwd_noalloc"]
+NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024  # FNA2_NOALLOC_SCRATCH_BYTES
 
 
 class Fna2Tensor(ctypes.Structure):
@@ -101,6 +102,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.fna2_fwd.restype = ctypes.c_int
     lib.fna2_bwd.argtypes = [ctypes.POINTER(Fna2BwdArgs), ctypes.c_void_p]
     lib.fna2_bwd.restype = ctypes.c_int
+    lib.fna2_bwd_noalloc.argtypes = [ctypes.POINTER(Fna2BwdArgs), ctypes.c_void_p]
+    lib.fna2_bwd_noalloc.restype = ctypes.c_int
     lib.fna2_bwd_workspace_size.argtypes = [ctypes.POINTER(Fna2Problem)]
     lib.fna2_bwd_workspace_size.restype = ctypes.c_size_t
     lib.fna2_last_error.argtypes = []

@@ -319,3 +319,6 @@ extern "C" int fna2_bwd(const Fna2BwdArgs* a, void* stream) {
                        reinterpret_cast<cudaEvent_t*>(a->launch_events)));
   return FNA2_OK;
 }
+
+// The no-allocation backward entry point (fna2_bwd_noalloc) and its static scratch.
+#include "fna2_noalloc.cu"

@@ -114,6 +114,21 @@ size_t fna2_bwd_workspace_size(const Fna2Problem* prob);
  * Replaces _fna2_backward / _fna2_backward_varlen. */
 int fna2_bwd(const Fna2BwdArgs* args, void* stream);
 
+/* Size of the device scratch array behind fna2_bwd_noalloc (32 MiB per GPU). */
+#define FNA2_NOALLOC_SCRATCH_BYTES (32 * 1024 * 1024)
+
+/* Backward for callers that cannot allocate device memory (no counterpart in
+ * the reference, which always allocates through PyTorch).  Same arguments and
+ * results as fna2_bwd, but args->workspace / workspace_bytes are ignored: the
+ * scratch (8 bytes per query row and head) comes from a static device array of
+ * FNA2_NOALLOC_SCRATCH_BYTES held by every GPU that loads the library until
+ * exit.  Larger problems return FNA2_ERR_WORKSPACE.  The first call on each
+ * device looks the array up (cudaGetSymbolAddress); make it before any stream
+ * capture.  All calls on a device share the array: calls whose GPU work
+ * overlaps race on it, so order them on one stream.  Calls no cudaMalloc or
+ * cudaFree. */
+int fna2_bwd_noalloc(const Fna2BwdArgs* args, void* stream);
+
 /* Message of the last failed call on this host thread ("" if none). */
 const char* fna2_last_error(void);
 
