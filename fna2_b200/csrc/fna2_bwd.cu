@@ -139,6 +139,17 @@ __device__ __forceinline__ uint32_t r_layout_of(int rp) {
 // ---------------------------------------------------------------------------
 // dK / dV / dR_k  (KV-stationary)
 // ---------------------------------------------------------------------------
+// Per query tile: S^T = K Q^T (+ R_k R~_q^T) and dP^T = V dO^T as full 128x128
+// MMAs; eight softmax-gradient warps (two warpgroups; thread = key row = TMEM
+// lane) each take 64 of the 128 query columns, load all of their S^T and dP^T
+// values before computing, and write P^T and dS^T back as bf16 into the first
+// half of their OWN column range (so no warp overwrites columns another warp
+// still has to read).  Then dV += P^T dO, dK += dS^T Q and the dR_k tile
+// dS^T R~_q run as TS-form MMAs reading P^T / dS^T from TMEM.
+// TMEM columns: dV [0,128) dK [128,256) S^T [256,384) dP^T [384,512).
+// P^T of query columns [64w, 64w+64) sits at S^T columns [64w, 64w+32), dS^T
+// likewise in dP^T; the dR_k tile uses dP^T columns [32, 32+r_pad), which
+// warpgroup 0 folds into registers before the next dP^T overwrites them.
 template <int D, int RP>
 struct DkdvSmem {
   static constexpr int kTile = 128 * D * 2;
@@ -156,7 +167,7 @@ struct DkdvSmem {
   static constexpr int oRq1 = align(oRq0 + kR);
   static constexpr int oVec = align(oRq1 + kR);  // [2 stages][lse2 128 | delta 128] floats
   static constexpr int oBar = oVec + 2 * 256 * 4;
-  static constexpr int kNumBars = 16;
+  static constexpr int kNumBars = 20;
   static constexpr int oMisc = oBar + kNumBars * 8;
   static constexpr int kTotal = oMisc + 16 + 1024;
 };
@@ -170,13 +181,15 @@ enum DkdvBar {
   kAPrep = 7,     // +stage
   kAStFull = 9,
   kAPReady = 10,
-  kADrk = 11,
-  kATmemFree = 12,
+  kADrkFull = 11,
+  kADrkFree = 12,
   kAAllDone = 13,
 };
 
+constexpr int kDkdvThreads = 352;  // 8 softmax-gradient warps, producer, MMA, prep
+
 template <int D, int RP>
-__global__ void __launch_bounds__(224, 1)
+__global__ void __launch_bounds__(kDkdvThreads, 1)
     fna2_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDo,
                          const __grid_constant__ CUtensorMap tmRq, const __grid_constant__ CUtensorMap tmRk,
@@ -228,14 +241,14 @@ __global__ void __launch_bounds__(224, 1)
       mbar_init(&bars[kAPrep + s], 32);
     }
     mbar_init(&bars[kAStFull], 1);
-    mbar_init(&bars[kAPReady], 128);
-    mbar_init(&bars[kADrk], 1);
-    mbar_init(&bars[kATmemFree], 128);
+    mbar_init(&bars[kAPReady], 256);
+    mbar_init(&bars[kADrkFull], 1);
+    mbar_init(&bars[kADrkFree], 256);
     mbar_init(&bars[kAAllDone], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -243,10 +256,11 @@ __global__ void __launch_bounds__(224, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns
-  const uint32_t tDV = tmem + 0, tDK = tmem + 128, tS = tmem + 256, tDP = tmem + 384, tDRK = tmem + 256 + 64;
+  const uint32_t tDV = tmem + 0, tDK = tmem + 128, tS = tmem + 256, tDP = tmem + 384, tDRK = tmem + 384 + 32;
+  // TMEM column of the packed bf16 operand for the 16 query rows of k-step kk
+  auto packed_col = [](int kk) { return (kk < 4 ? 0 : 64) + (kk & 3) * 8; };
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
@@ -287,7 +301,7 @@ __global__ void __launch_bounds__(224, 1)
         }
       }
     }
-  } else if (warp == 6) {
+  } else if (warp == 10) {
     // ------------------------------------------------------------ prep: lse2/Delta rows, R~_q
     int it = 0;
     bool ok = true;
@@ -316,90 +330,100 @@ __global__ void __launch_bounds__(224, 1)
         mbar_arrive(&bars[kAPrep + s]);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_st = make_idesc_bf16(128, 128, 0, 0);    // S^T, dP^T
-      constexpr uint32_t idesc_acc = make_idesc_bf16(128, D, 0, 1);     // dV, dK (A in TMEM, B MN-major)
-      constexpr uint32_t idesc_drk = make_idesc_bf16(128, RP, 0, 1);    // dR_k tile
+      constexpr uint32_t idesc_st = make_idesc_bf16(128, 128, 0, 0);   // S^T, dP^T
+      constexpr uint32_t idesc_acc = make_idesc_bf16(128, D, 0, 1);    // dV, dK (A in TMEM, B MN-major)
+      constexpr uint32_t idesc_drk = make_idesc_bf16(128, RP, 0, 1);   // dR_k tile
       const uint32_t r_layout = r_layout_of(RP);
       const uint32_t r_sbo = 8 * RP * 2;
       const uint32_t sK = smem_u32(smem + L::oK), sV = smem_u32(smem + L::oV), sRk = smem_u32(smem + L::oRk);
+      auto graph_of = [&](int it) { return it / n_it < gh; };
       bool ok = mbar_wait(&bars[kAKV], 0, abort_flag, 501);
-      int it = 0;
-      for (int e = 0; ok && e < g; ++e) {
-        const bool graph = e < gh;
-        if (graph && !mbar_wait(&bars[kARkFull], e & 1, abort_flag, 502)) break;
-        for (int mi = 0; mi < n_it; ++mi, ++it) {
-          const int s = it & 1;
-          const uint32_t sQ = smem_u32(smem + (s ? L::oQ1 : L::oQ0));
-          const uint32_t sDo = smem_u32(smem + (s ? L::oDo1 : L::oDo0));
-          const uint32_t sRq = smem_u32(smem + (s ? L::oRq1 : L::oRq0));
-          if (!mbar_wait(&bars[kAQFull + s], (it >> 1) & 1, abort_flag, 503) ||
-              !mbar_wait(&bars[kAPrep + s], (it >> 1) & 1, abort_flag, 504) ||
-              (it > 0 && !mbar_wait(&bars[kATmemFree], (it - 1) & 1, abort_flag, 505))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          // S^T = K Q^T (+ R_k R~_q^T), dP^T = V dO^T
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * L::kChunk + (kk & 3) * 32;
-            mma_ss(tS, make_sdesc(sK + off, 16, 1024, kSwizzle128B), make_sdesc(sQ + off, 16, 1024, kSwizzle128B),
-                   idesc_st, kk > 0);
-          }
-          if (graph) {
-#pragma unroll
-            for (int kk = 0; kk < RP / 16; ++kk)
-              mma_ss(tS, make_sdesc(sRk + kk * 32, 16, r_sbo, r_layout), make_sdesc(sRq + kk * 32, 16, r_sbo, r_layout),
-                     idesc_st, 1);
-          }
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * L::kChunk + (kk & 3) * 32;
-            mma_ss(tDP, make_sdesc(sV + off, 16, 1024, kSwizzle128B), make_sdesc(sDo + off, 16, 1024, kSwizzle128B),
-                   idesc_st, kk > 0);
-          }
-          mma_commit(&bars[kAStFull]);
-          if (!mbar_wait(&bars[kAPReady], it & 1, abort_flag, 506)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          // dV += P^T dO ; dK += dS^T Q   (K = 128 query rows, 8 steps of 16)
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            mma_ts(tDV, tS + kk * 8, make_sdesc(sDo + kk * 2048, L::kChunk, 1024, kSwizzle128B), idesc_acc,
-                   (it > 0 || kk > 0) ? 1u : 0u);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            mma_ts(tDK, tDP + kk * 8, make_sdesc(sQ + kk * 2048, L::kChunk, 1024, kSwizzle128B), idesc_acc,
-                   (it > 0 || kk > 0) ? 1u : 0u);
-          if (graph) {
-            // dR_k tile = dS^T R~_q  (B MN-major: r_pad contiguous, rows of RP*2 bytes)
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk)
-              mma_ts(tDRK, tDP + kk * 8, make_sdesc(sRq + kk * 16 * RP * 2, 16, r_sbo, r_layout), idesc_drk,
-                     kk > 0 ? 1u : 0u);
-            mma_commit(&bars[kADrk]);
-          }
-          mma_commit(&bars[kAQEmpty + s]);
-          if (graph && mi == n_it - 1) mma_commit(&bars[kARkEmpty]);
+      int git = 0;
+      for (int it = 0; ok && it < total_it; ++it) {
+        const int s = it & 1;
+        const bool graph = graph_of(it);
+        const bool first_of_head = (it % n_it) == 0, last_of_head = (it % n_it) == n_it - 1;
+        const uint32_t sQ = smem_u32(smem + (s ? L::oQ1 : L::oQ0));
+        const uint32_t sDo = smem_u32(smem + (s ? L::oDo1 : L::oDo0));
+        const uint32_t sRq = smem_u32(smem + (s ? L::oRq1 : L::oRq0));
+        if (!mbar_wait(&bars[kAQFull + s], (it >> 1) & 1, abort_flag, 503) ||
+            !mbar_wait(&bars[kAPrep + s], (it >> 1) & 1, abort_flag, 504) ||
+            (graph && first_of_head && !mbar_wait(&bars[kARkFull], (it / n_it) & 1, abort_flag, 502))) {
+          ok = false;
+          break;
         }
+        tc_fence_after();
+        // S^T = K Q^T (+ R_k R~_q^T)
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * L::kChunk + (kk & 3) * 32;
+          mma_ss(tS, make_sdesc(sK + off, 16, 1024, kSwizzle128B), make_sdesc(sQ + off, 16, 1024, kSwizzle128B),
+                 idesc_st, kk > 0);
+        }
+        if (graph) {
+#pragma unroll
+          for (int kk = 0; kk < RP / 16; ++kk)
+            mma_ss(tS, make_sdesc(sRk + kk * 32, 16, r_sbo, r_layout), make_sdesc(sRq + kk * 32, 16, r_sbo, r_layout),
+                   idesc_st, 1);
+          if (last_of_head) mma_commit(&bars[kARkEmpty]);
+        }
+        // dP^T = V dO^T overwrites the previous dR_k tile: wait until it was folded
+        if (it > 0 && !mbar_wait(&bars[kADrkFree], (it - 1) & 1, abort_flag, 505)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * L::kChunk + (kk & 3) * 32;
+          mma_ss(tDP, make_sdesc(sV + off, 16, 1024, kSwizzle128B), make_sdesc(sDo + off, 16, 1024, kSwizzle128B),
+                 idesc_st, kk > 0);
+        }
+        mma_commit(&bars[kAStFull]);
+        if (!mbar_wait(&bars[kAPReady], it & 1, abort_flag, 506)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // dV += P^T dO ; dK += dS^T Q   (K = 128 query rows, 8 steps of 16)
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_ts(tDV, tS + packed_col(kk), make_sdesc(sDo + kk * 2048, L::kChunk, 1024, kSwizzle128B), idesc_acc,
+                 (it > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_ts(tDK, tDP + packed_col(kk), make_sdesc(sQ + kk * 2048, L::kChunk, 1024, kSwizzle128B), idesc_acc,
+                 (it > 0 || kk > 0) ? 1u : 0u);
+        if (graph) {
+          // dR_k tile = dS^T R~_q  (B MN-major: r_pad contiguous, rows of RP*2 bytes)
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_ts(tDRK, tDP + packed_col(kk), make_sdesc(sRq + kk * 16 * RP * 2, 16, r_sbo, r_layout), idesc_drk,
+                   kk > 0 ? 1u : 0u);
+          mma_commit(&bars[kADrkFull]);
+          ++git;
+        }
+        mma_commit(&bars[kAQEmpty + s]);
       }
       if (ok) mma_commit(&bars[kAAllDone]);
     }
   } else {
-    // ------------------------------------------------------------ softmax-gradient warps 0-3 (key rows)
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    const int kv_local = n0 + tid;
+    // ------------------------------------------------------------ softmax-gradient warps 0-7
+    const int wg = warp >> 2;  // warpgroup: query columns [64*wg, 64*wg+64) of every tile
+    const int hh = wg;         // epilogue: D-column half stored by this warpgroup
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int t = tid & 127;   // key row within the tile (TMEM lane)
+    const int kv_local = n0 + t;
     const bool kv_valid = kv_local < si.len_k;
     const float sl2 = P.scale_log2;
     const int64_t krow = si.k_start + kv_local;
-    float drk_acc[RP];
+    const uint32_t tSw = tS + lane_base + 64 * wg, tDPw = tDP + lane_base + 64 * wg;
+    float drk_acc[RP / 2];  // this warpgroup's dR_k columns [wg*RP/2, (wg+1)*RP/2)
 #pragma unroll
-    for (int i = 0; i < RP; ++i) drk_acc[i] = 0.f;
+    for (int i = 0; i < RP / 2; ++i) drk_acc[i] = 0.f;
     int it = 0, git = 0;
     bool ok = true;
     for (int e = 0; ok && e < g; ++e) {
@@ -409,67 +433,82 @@ __global__ void __launch_bounds__(224, 1)
         const int s = it & 1;
         const int m0 = (m_start + mi) * kBlockM;
         const float* lv = vec + s * 256;
-        if (!mbar_wait(&bars[kAStFull], it & 1, abort_flag, 701) ||
-            !mbar_wait(&bars[kAPrep + s], (it >> 1) & 1, abort_flag, 702)) {
+        // valid query columns q in [q_lo, q_hi) (tile-relative) for this key row
+        const int q_hi = kv_valid ? (si.len_q - m0) : 0;
+        const int q_lo = P.causal ? (kv_local - m0) : 0;
+        if (!mbar_wait(&bars[kAPrep + s], (it >> 1) & 1, abort_flag, 702) ||
+            !mbar_wait(&bars[kAStFull], it & 1, abort_flag, 701)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        // valid query columns q in [q_lo, q_hi) for this key row
-        const int q_hi = kv_valid ? (si.len_q - m0) : 0;
-        const int q_lo = P.causal ? (kv_local - m0) : 0;
+        // two 32-column chunks; chunk c's packed output lands in columns
+        // [16c, 16c+16) of this warp's range, which it has already read
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t sv[32], dp[32];
-          tmem_ld32(tS + lane_base + 32 * c, sv);
-          tmem_ld32(tDP + lane_base + 32 * c, dp);
+          tmem_ld32(tSw + 32 * c, sv);
+          tmem_ld32(tDPw + 32 * c, dp);
           tmem_ld_wait32(sv);
           tmem_ld_wait32(dp);
+          const int qb = 64 * wg + 32 * c;
+          // masked query columns get -inf exponents (ex2(-inf) = 0)
+          if (!((qb >= q_lo) && (qb + 32 <= q_hi))) {
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+              const int qi = qb + k;
+              if (!(qi >= q_lo && qi < q_hi)) sv[k] = __float_as_uint(-INFINITY);
+            }
+          }
+          float lq[32], dl[32];
+#pragma unroll
+          for (int k = 0; k < 32; k += 4) {
+            const float4 l4 = *reinterpret_cast<const float4*>(&lv[qb + k]);
+            const float4 d4 = *reinterpret_cast<const float4*>(&lv[128 + qb + k]);
+            lq[k] = l4.x; lq[k + 1] = l4.y; lq[k + 2] = l4.z; lq[k + 3] = l4.w;
+            dl[k] = d4.x; dl[k + 1] = d4.y; dl[k + 2] = d4.z; dl[k + 3] = d4.w;
+          }
           uint32_t pp[16], dd[16];
 #pragma unroll
           for (int k = 0; k < 32; k += 2) {
-            const int q0i = 32 * c + k;
-            const bool v0 = q0i >= q_lo && q0i < q_hi;
-            const bool v1 = q0i + 1 >= q_lo && q0i + 1 < q_hi;
-            const float p0 = v0 ? ex2(fmaf(__uint_as_float(sv[k]), sl2, -lv[q0i])) : 0.f;
-            const float p1 = v1 ? ex2(fmaf(__uint_as_float(sv[k + 1]), sl2, -lv[q0i + 1])) : 0.f;
-            const float d0 = p0 * (__uint_as_float(dp[k]) - lv[128 + q0i]);
-            const float d1 = p1 * (__uint_as_float(dp[k + 1]) - lv[128 + q0i + 1]);
+            const float p0 = ex2(fmaf(__uint_as_float(sv[k]), sl2, -lq[k]));
+            const float p1 = ex2(fmaf(__uint_as_float(sv[k + 1]), sl2, -lq[k + 1]));
             pp[k >> 1] = pack_bf16(p0, p1);
-            dd[k >> 1] = pack_bf16(d0, d1);
+            dd[k >> 1] = pack_bf16(p0 * (__uint_as_float(dp[k]) - dl[k]), p1 * (__uint_as_float(dp[k + 1]) - dl[k + 1]));
           }
-          tmem_st16(tS + lane_base + 16 * c, pp);
-          tmem_st16(tDP + lane_base + 16 * c, dd);
+          tmem_st16(tSw + 16 * c, pp);
+          tmem_st16(tDPw + 16 * c, dd);
         }
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&bars[kAPReady]);
+        // each warpgroup folds its RP/2 columns of the dR_k tile into registers
         if (graph) {
-          if (!mbar_wait(&bars[kADrk], git & 1, abort_flag, 703)) {
+          if (!mbar_wait(&bars[kADrkFull], git & 1, abort_flag, 703)) {
             ok = false;
             break;
           }
           ++git;
           tc_fence_after();
-          uint32_t rv[32];
+          uint32_t rv[16];
           if (RP == 16) {
-            tmem_ld16(tDRK + lane_base, rv);
-            tmem_ld_wait16(rv);
+            tmem_ld8(tDRK + lane_base + 8 * wg, rv);
+            tmem_ld_wait8(rv);
           } else {
-            tmem_ld32(tDRK + lane_base, rv);
-            tmem_ld_wait32(rv);
+            tmem_ld16(tDRK + lane_base + 16 * wg, rv);
+            tmem_ld_wait16(rv);
           }
 #pragma unroll
-          for (int i = 0; i < RP; ++i) drk_acc[i] += __uint_as_float(rv[i]);
+          for (int i = 0; i < RP / 2; ++i) drk_acc[i] += __uint_as_float(rv[i]);
         }
         tc_fence_before();
-        mbar_arrive(&bars[kATmemFree]);
+        mbar_arrive(&bars[kADrkFree]);
         if (graph && mi == n_it - 1) {
           if (kv_valid) {
-            __nv_bfloat16* dst = p.drk + si.b * p.drk_sb + h * p.drk_sh + krow * p.drk_sr;
+            __nv_bfloat16* dst = p.drk + si.b * p.drk_sb + h * p.drk_sh + krow * p.drk_sr + wg * (RP / 2);
 #pragma unroll
-            for (int c = 0; c < RP; c += 8) {
-              if (c < P.rank) {
+            for (int c = 0; c < RP / 2; c += 8) {
+              if (wg * (RP / 2) + c < P.rank) {
                 uint4 w;
                 uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
 #pragma unroll
@@ -480,21 +519,23 @@ __global__ void __launch_bounds__(224, 1)
             }
           }
 #pragma unroll
-          for (int i = 0; i < RP; ++i) drk_acc[i] = 0.f;
+          for (int i = 0; i < RP / 2; ++i) drk_acc[i] = 0.f;
         }
       }
     }
     if (ok && mbar_wait(&bars[kAAllDone], 0, abort_flag, 704)) {
       tc_fence_after();
-      __nv_bfloat16* dvrow = p.dv + si.b * p.dv_sb + hk * p.dv_sh + krow * p.dv_sr;
-      __nv_bfloat16* dkrow = p.dk + si.b * p.dk_sb + hk * p.dk_sh + krow * p.dk_sr;
+      // each warpgroup stores its 64 of the D columns of dV and dK (D = 128) or 32 (D = 64)
+      constexpr int kCols = D / 2;
+      __nv_bfloat16* dvrow = p.dv + si.b * p.dv_sb + hk * p.dv_sh + krow * p.dv_sr + hh * kCols;
+      __nv_bfloat16* dkrow = p.dk + si.b * p.dk_sb + hk * p.dk_sh + krow * p.dk_sr + hh * kCols;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < kCols / 32; ++c) {
         uint32_t v[32];
-        tmem_ld32(tDV + lane_base + 32 * c, v);
+        tmem_ld32(tDV + lane_base + hh * kCols + 32 * c, v);
         tmem_ld_wait32(v);
         if (kv_valid) store_row32(dvrow + 32 * c, v, 1.f);
-        tmem_ld32(tDK + lane_base + 32 * c, v);
+        tmem_ld32(tDK + lane_base + hh * kCols + 32 * c, v);
         tmem_ld_wait32(v);
         if (kv_valid) store_row32(dkrow + 32 * c, v, scale);
       }
@@ -503,7 +544,7 @@ __global__ void __launch_bounds__(224, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -512,6 +553,12 @@ __global__ void __launch_bounds__(224, 1)
 // ---------------------------------------------------------------------------
 // dQ / dR_q / d_gs  (Q-stationary)
 // ---------------------------------------------------------------------------
+// One CTA per (128-row query tile, head, sequence), looping over the causally
+// visible key tiles: S = Q K^T (+ R~_q R_k^T), dP = dO V^T (full 128x128 MMAs)
+// -> eight softmax-gradient warps (thread = query row = TMEM lane; warpgroup w
+// takes key columns [64w, 64w+64)) write dS as bf16 into the first half of
+// their own column range -> dQ += dS K, dR_q += dS R_k (TS form).
+// TMEM columns: dQ [0,128) dR_q [128,128+r_pad) S [256,384) dP [384,512).
 template <int D, int RP>
 struct DqSmem {
   static constexpr int kTile = 128 * D * 2;
@@ -528,7 +575,7 @@ struct DqSmem {
   static constexpr int oRk0 = align(oV1 + kTile);
   static constexpr int oRk1 = align(oRk0 + kR);
   static constexpr int oBar = align(oRk1 + kR);
-  static constexpr int kNumBars = 12;
+  static constexpr int kNumBars = 16;
   static constexpr int oMisc = oBar + kNumBars * 8;
   static constexpr int kTotal = oMisc + 16 + 1024;
 };
@@ -543,8 +590,10 @@ enum DqBar {
   kBAllDone = 8,
 };
 
+constexpr int kDqThreads = 320;  // 8 softmax-gradient warps, producer, MMA
+
 template <int D, int RP>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kDqThreads, 1)
     fna2_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDo,
                        const __grid_constant__ CUtensorMap tmRq, const __grid_constant__ CUtensorMap tmRk,
@@ -588,12 +637,12 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&bars[kBKvEmpty + s], 1);
     }
     mbar_init(&bars[kBStFull], 1);
-    mbar_init(&bars[kBPReady], 128);
+    mbar_init(&bars[kBPReady], 256);
     mbar_init(&bars[kBAllDone], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -602,8 +651,11 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tDQ = tmem + 0, tDRQ = tmem + 128, tS = tmem + 256, tDP = tmem + 384;
+  // TMEM column (relative to S) of the packed bf16 dS for the 16 keys of k-step kk
+  auto packed_col = [](int kk) { return (kk < 4 ? 0 : 64) + (kk & 3) * 8; };
 
-  if (warp == 4) {
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
@@ -630,7 +682,8 @@ __global__ void __launch_bounds__(192, 1)
         if (graph) tma_load_4d(smem + (s ? L::oRk1 : L::oRk0), &tmRk, &bars[kBKvFull + s], 0, krow, h, si.b);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, 0, 0);
       constexpr uint32_t idesc_dq = make_idesc_bf16(128, D, 0, 1);
@@ -647,6 +700,7 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t sRk = smem_u32(smem + (s ? L::oRk1 : L::oRk0));
         if (!mbar_wait(&bars[kBKvFull + s], (j >> 1) & 1, abort_flag, 903)) break;
         tc_fence_after();
+        // S and dP overwrite the previous tile's dS, read by the dQ MMAs issued before (in order)
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * L::kChunk + (kk & 3) * 32;
@@ -668,15 +722,14 @@ __global__ void __launch_bounds__(192, 1)
         mma_commit(&bars[kBStFull]);
         if (!mbar_wait(&bars[kBPReady], j & 1, abort_flag, 904)) break;
         tc_fence_after();
-        // dQ += dS K ; dR_q += dS R_k  (dS in TMEM over the S columns)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          mma_ts(tDQ, tS + kk * 8, make_sdesc(sK + kk * 2048, L::kChunk, 1024, kSwizzle128B), idesc_dq,
+          mma_ts(tDQ, tS + packed_col(kk), make_sdesc(sK + kk * 2048, L::kChunk, 1024, kSwizzle128B), idesc_dq,
                  (j > 0 || kk > 0) ? 1u : 0u);
         if (graph) {
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            mma_ts(tDRQ, tS + kk * 8, make_sdesc(sRk + kk * 16 * RP * 2, 16, r_sbo, r_layout), idesc_drq,
+            mma_ts(tDRQ, tS + packed_col(kk), make_sdesc(sRk + kk * 16 * RP * 2, 16, r_sbo, r_layout), idesc_drq,
                    (j > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(&bars[kBKvEmpty + s]);
@@ -684,9 +737,11 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax-gradient warps 0-3 (query rows)
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    const int q_local = q0 + tid;
+    // ------------------------------------------------------------ softmax-gradient warps 0-7 (query rows)
+    const int wg = warp >> 2;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int t = tid & 127;
+    const int q_local = q0 + t;
     const bool row_ok = q_local < si.len_q;
     const int64_t row = si.q_start + q_local;
     const int64_t widx = (static_cast<int64_t>(si.b) * P.heads + h) * p.ws_sbh + row;
@@ -695,37 +750,46 @@ __global__ void __launch_bounds__(192, 1)
     const float sl2 = P.scale_log2;
     const int limit = row_ok ? (P.causal ? min(si.len_k, q_local + 1) : si.len_k) : 0;
     bool ok = true;
-    if (graph) {
+    if (graph && wg == 0) {
       ok = mbar_wait(&bars[kBQFull], 0, abort_flag, 1001);
       if (ok) {
-        scale_rows_inplace<RP>(smem + L::oRq, tid, __ldg(P.gs + h) / scale);
+        scale_rows_inplace<RP>(smem + L::oRq, t, __ldg(P.gs + h) / scale);
         fence_proxy_async_smem();
       }
       mbar_arrive(&bars[kBRqReady]);
     }
+    const uint32_t tSw = tS + lane_base + 64 * wg, tDPw = tDP + lane_base + 64 * wg;
     for (int j = 0; ok && j < n_tiles; ++j) {
       if (!mbar_wait(&bars[kBStFull], j & 1, abort_flag, 1002)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const int nvalid = limit - j * kBlockN;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t sv[32], dp[32];
-        tmem_ld32(tS + lane_base + 32 * c, sv);
-        tmem_ld32(tDP + lane_base + 32 * c, dp);
+        tmem_ld32(tSw + 32 * c, sv);
+        tmem_ld32(tDPw + 32 * c, dp);
         tmem_ld_wait32(sv);
         tmem_ld_wait32(dp);
+        const int nvalid = limit - (j * kBlockN + 64 * wg + 32 * c);
         uint32_t dd[16];
+        if (nvalid >= 32) {
 #pragma unroll
-        for (int k = 0; k < 32; k += 2) {
-          const int kv = 32 * c + k;
-          const float p0 = kv < nvalid ? ex2(fmaf(__uint_as_float(sv[k]), sl2, -lse2)) : 0.f;
-          const float p1 = kv + 1 < nvalid ? ex2(fmaf(__uint_as_float(sv[k + 1]), sl2, -lse2)) : 0.f;
-          dd[k >> 1] = pack_bf16(p0 * (__uint_as_float(dp[k]) - delta), p1 * (__uint_as_float(dp[k + 1]) - delta));
+          for (int k = 0; k < 32; k += 2) {
+            const float p0 = ex2(fmaf(__uint_as_float(sv[k]), sl2, -lse2));
+            const float p1 = ex2(fmaf(__uint_as_float(sv[k + 1]), sl2, -lse2));
+            dd[k >> 1] = pack_bf16(p0 * (__uint_as_float(dp[k]) - delta), p1 * (__uint_as_float(dp[k + 1]) - delta));
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 32; k += 2) {
+            const float p0 = ex2(k < nvalid ? fmaf(__uint_as_float(sv[k]), sl2, -lse2) : -INFINITY);
+            const float p1 = ex2(k + 1 < nvalid ? fmaf(__uint_as_float(sv[k + 1]), sl2, -lse2) : -INFINITY);
+            dd[k >> 1] = pack_bf16(p0 * (__uint_as_float(dp[k]) - delta), p1 * (__uint_as_float(dp[k + 1]) - delta));
+          }
         }
-        tmem_st16(tS + lane_base + 16 * c, dd);
+        tmem_st16(tSw + 16 * c, dd);  // columns this warp has already read
       }
       tmem_st_wait();
       tc_fence_before();
@@ -733,15 +797,16 @@ __global__ void __launch_bounds__(192, 1)
     }
     if (ok && mbar_wait(&bars[kBAllDone], 0, abort_flag, 1003)) {
       tc_fence_after();
-      __nv_bfloat16* dqrow = p.dq + si.b * p.dq_sb + h * p.dq_sh + row * p.dq_sr;
+      constexpr int kCols = D / 2;
+      __nv_bfloat16* dqrow = p.dq + si.b * p.dq_sb + h * p.dq_sh + row * p.dq_sr + wg * kCols;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < kCols / 32; ++c) {
         uint32_t v[32];
-        tmem_ld32(tDQ + lane_base + 32 * c, v);
+        tmem_ld32(tDQ + lane_base + wg * kCols + 32 * c, v);
         tmem_ld_wait32(v);
         if (row_ok) store_row32(dqrow + 32 * c, v, scale);
       }
-      if (graph) {
+      if (graph && wg == 0) {
         uint32_t rv[32];
         if (RP == 16) {
           tmem_ld16(tDRQ + lane_base, rv);
@@ -782,7 +847,7 @@ __global__ void __launch_bounds__(192, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -814,7 +879,7 @@ cudaError_t launch_bwd_t(const CUtensorMap& q, const CUtensorMap& k, const CUten
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
     if (e != cudaSuccess) return e;
     dim3 grid(p.n_nblocks, p.prob.heads_kv, p.batch);
-    kern<<<grid, 224, L::kTotal, stream>>>(q, k, v, dO, rq, rk, p);
+    kern<<<grid, kDkdvThreads, L::kTotal, stream>>>(q, k, v, dO, rq, rk, p);
     e = cudaGetLastError();
     if (e == cudaSuccess && ev) e = cudaEventRecord(ev[2], stream);
     if (e != cudaSuccess) return e;
@@ -825,7 +890,7 @@ cudaError_t launch_bwd_t(const CUtensorMap& q, const CUtensorMap& k, const CUten
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
     if (e != cudaSuccess) return e;
     dim3 grid(p.n_mblocks, p.prob.heads, p.batch);
-    kern<<<grid, 192, L::kTotal, stream>>>(q, k, v, dO, rq, rk, p);
+    kern<<<grid, kDqThreads, L::kTotal, stream>>>(q, k, v, dO, rq, rk, p);
     e = cudaGetLastError();
     if (e == cudaSuccess && ev) e = cudaEventRecord(ev[3], stream);
     if (e != cudaSuccess) return e;

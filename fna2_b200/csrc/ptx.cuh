@@ -214,11 +214,17 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
       : FNA2_R8(0), FNA2_R8(8)
       : "r"(taddr));
 }
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];" : FNA2_R8(0) : "r"(taddr));
+}
 // Wait for outstanding tcgen05.ld; the registers are tied in so that no use
 // of them can be scheduled before the wait.
 __device__ __forceinline__ void tmem_ld_wait32(uint32_t* r) {
   asm volatile("tcgen05.wait::ld.sync.aligned;"
                : FNA2_W8(0), FNA2_W8(8), FNA2_W8(16), FNA2_W8(24)::"memory");
+}
+__device__ __forceinline__ void tmem_ld_wait8(uint32_t* r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : FNA2_W8(0)::"memory");
 }
 __device__ __forceinline__ void tmem_ld_wait16(uint32_t* r) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" : FNA2_W8(0), FNA2_W8(8)::"memory");
@@ -256,9 +262,11 @@ __device__ __forceinline__ float lg2(float x) {
   asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// Round two floats to bf16 (round-to-nearest-even) and pack them, lo in bits 0..15.
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
