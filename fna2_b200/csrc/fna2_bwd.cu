@@ -141,11 +141,12 @@ __device__ __forceinline__ uint32_t r_layout_of(int rp) {
 // ---------------------------------------------------------------------------
 // Per query tile: S^T = K Q^T (+ R_k R~_q^T) and dP^T = V dO^T as full 128x128
 // MMAs; eight softmax-gradient warps (two warpgroups; thread = key row = TMEM
-// lane) each take 64 of the 128 query columns, load all of their S^T and dP^T
-// values before computing, and write P^T and dS^T back as bf16 into the first
-// half of their OWN column range (so no warp overwrites columns another warp
-// still has to read).  Then dV += P^T dO, dK += dS^T Q and the dR_k tile
-// dS^T R~_q run as TS-form MMAs reading P^T / dS^T from TMEM.
+// lane) each take 64 of the 128 query columns and write P^T and dS^T back as
+// bf16 into the first half of their OWN column range (so no warp overwrites
+// columns another warp still has to read).  The hand-offs are split so the
+// phases overlap: the warps form P^T while the tensor core computes dP^T, and
+// dV += P^T dO runs while they form dS^T; then dK += dS^T Q and the dR_k tile
+// dS^T R~_q (TS-form MMAs reading P^T / dS^T from TMEM).
 // TMEM columns: dV [0,128) dK [128,256) S^T [256,384) dP^T [384,512).
 // P^T of query columns [64w, 64w+64) sits at S^T columns [64w, 64w+32), dS^T
 // likewise in dP^T; the dR_k tile uses dP^T columns [32, 32+r_pad), which
@@ -179,11 +180,13 @@ enum DkdvBar {
   kAQFull = 3,    // +stage
   kAQEmpty = 5,   // +stage
   kAPrep = 7,     // +stage
-  kAStFull = 9,
+  kASFull = 9,
   kAPReady = 10,
   kADrkFull = 11,
   kADrkFree = 12,
   kAAllDone = 13,
+  kADPFull = 14,
+  kADsReady = 15,
 };
 
 constexpr int kDkdvThreads = 352;  // 8 softmax-gradient warps, producer, MMA, prep
@@ -240,8 +243,10 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
       mbar_init(&bars[kAQEmpty + s], 1);
       mbar_init(&bars[kAPrep + s], 32);
     }
-    mbar_init(&bars[kAStFull], 1);
+    mbar_init(&bars[kASFull], 1);
+    mbar_init(&bars[kADPFull], 1);
     mbar_init(&bars[kAPReady], 256);
+    mbar_init(&bars[kADsReady], 256);
     mbar_init(&bars[kADrkFull], 1);
     mbar_init(&bars[kADrkFree], 256);
     mbar_init(&bars[kAAllDone], 1);
@@ -370,6 +375,7 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
                    idesc_st, 1);
           if (last_of_head) mma_commit(&bars[kARkEmpty]);
         }
+        mma_commit(&bars[kASFull]);
         // dP^T = V dO^T overwrites the previous dR_k tile: wait until it was folded
         if (it > 0 && !mbar_wait(&bars[kADrkFree], (it - 1) & 1, abort_flag, 505)) {
           ok = false;
@@ -382,17 +388,23 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
           mma_ss(tDP, make_sdesc(sV + off, 16, 1024, kSwizzle128B), make_sdesc(sDo + off, 16, 1024, kSwizzle128B),
                  idesc_st, kk > 0);
         }
-        mma_commit(&bars[kAStFull]);
+        mma_commit(&bars[kADPFull]);
         if (!mbar_wait(&bars[kAPReady], it & 1, abort_flag, 506)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        // dV += P^T dO ; dK += dS^T Q   (K = 128 query rows, 8 steps of 16)
+        // dV += P^T dO   (K = 128 query rows, 8 steps of 16)
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           mma_ts(tDV, tS + packed_col(kk), make_sdesc(sDo + kk * 2048, L::kChunk, 1024, kSwizzle128B), idesc_acc,
                  (it > 0 || kk > 0) ? 1u : 0u);
+        if (!mbar_wait(&bars[kADsReady], it & 1, abort_flag, 507)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // dK += dS^T Q
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           mma_ts(tDK, tDP + packed_col(kk), make_sdesc(sQ + kk * 2048, L::kChunk, 1024, kSwizzle128B), idesc_acc,
@@ -437,51 +449,71 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
         const int q_hi = kv_valid ? (si.len_q - m0) : 0;
         const int q_lo = P.causal ? (kv_local - m0) : 0;
         if (!mbar_wait(&bars[kAPrep + s], (it >> 1) & 1, abort_flag, 702) ||
-            !mbar_wait(&bars[kAStFull], it & 1, abort_flag, 701)) {
+            !mbar_wait(&bars[kASFull], it & 1, abort_flag, 701)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        // two 32-column chunks; chunk c's packed output lands in columns
+        // phase 1 (overlaps the dP^T MMA): P^T = exp2(S^T*c - LSE2) in two
+        // 32-column chunks; chunk c's packed output lands in columns
         // [16c, 16c+16) of this warp's range, which it has already read
-#pragma unroll 1
+        uint32_t pk[32];  // P as packed bf16 pairs, kept for phase 2
+#pragma unroll
         for (int c = 0; c < 2; ++c) {
-          uint32_t sv[32], dp[32];
+          uint32_t sv[32];
           tmem_ld32(tSw + 32 * c, sv);
-          tmem_ld32(tDPw + 32 * c, dp);
           tmem_ld_wait32(sv);
-          tmem_ld_wait32(dp);
           const int qb = 64 * wg + 32 * c;
-          // masked query columns get -inf exponents (ex2(-inf) = 0)
-          if (!((qb >= q_lo) && (qb + 32 <= q_hi))) {
+          if (!((qb >= q_lo) && (qb + 32 <= q_hi))) {  // masked columns: -inf exponent
 #pragma unroll
             for (int k = 0; k < 32; ++k) {
               const int qi = qb + k;
               if (!(qi >= q_lo && qi < q_hi)) sv[k] = __float_as_uint(-INFINITY);
             }
           }
-          float lq[32], dl[32];
 #pragma unroll
           for (int k = 0; k < 32; k += 4) {
             const float4 l4 = *reinterpret_cast<const float4*>(&lv[qb + k]);
-            const float4 d4 = *reinterpret_cast<const float4*>(&lv[128 + qb + k]);
-            lq[k] = l4.x; lq[k + 1] = l4.y; lq[k + 2] = l4.z; lq[k + 3] = l4.w;
-            dl[k] = d4.x; dl[k + 1] = d4.y; dl[k + 2] = d4.z; dl[k + 3] = d4.w;
+            const float p0 = ex2(fmaf(__uint_as_float(sv[k]), sl2, -l4.x));
+            const float p1 = ex2(fmaf(__uint_as_float(sv[k + 1]), sl2, -l4.y));
+            const float p2 = ex2(fmaf(__uint_as_float(sv[k + 2]), sl2, -l4.z));
+            const float p3 = ex2(fmaf(__uint_as_float(sv[k + 3]), sl2, -l4.w));
+            pk[16 * c + (k >> 1)] = pack_bf16(p0, p1);
+            pk[16 * c + (k >> 1) + 1] = pack_bf16(p2, p3);
           }
-          uint32_t pp[16], dd[16];
-#pragma unroll
-          for (int k = 0; k < 32; k += 2) {
-            const float p0 = ex2(fmaf(__uint_as_float(sv[k]), sl2, -lq[k]));
-            const float p1 = ex2(fmaf(__uint_as_float(sv[k + 1]), sl2, -lq[k + 1]));
-            pp[k >> 1] = pack_bf16(p0, p1);
-            dd[k >> 1] = pack_bf16(p0 * (__uint_as_float(dp[k]) - dl[k]), p1 * (__uint_as_float(dp[k + 1]) - dl[k + 1]));
-          }
-          tmem_st16(tSw + 16 * c, pp);
-          tmem_st16(tDPw + 16 * c, dd);
+          tmem_st16(tSw + 16 * c, pk + 16 * c);
         }
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&bars[kAPReady]);
+        // phase 2 (overlaps the dV MMA): dS^T = P^T (dP^T - Delta), with the
+        // same bf16-rounded P that the dV MMA consumes
+        if (!mbar_wait(&bars[kADPFull], it & 1, abort_flag, 704)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t dp[32];
+          tmem_ld32(tDPw + 32 * c, dp);
+          tmem_ld_wait32(dp);
+          const int qb = 64 * wg + 32 * c;
+          uint32_t dd[16];
+#pragma unroll
+          for (int k = 0; k < 32; k += 4) {
+            const float4 d4 = *reinterpret_cast<const float4*>(&lv[128 + qb + k]);
+            const uint32_t a = pk[16 * c + (k >> 1)], b = pk[16 * c + (k >> 1) + 1];
+            dd[k >> 1] = pack_bf16(__uint_as_float(a << 16) * (__uint_as_float(dp[k]) - d4.x),
+                                   __uint_as_float(a & 0xffff0000u) * (__uint_as_float(dp[k + 1]) - d4.y));
+            dd[(k >> 1) + 1] = pack_bf16(__uint_as_float(b << 16) * (__uint_as_float(dp[k + 2]) - d4.z),
+                                         __uint_as_float(b & 0xffff0000u) * (__uint_as_float(dp[k + 3]) - d4.w));
+          }
+          tmem_st16(tDPw + 16 * c, dd);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&bars[kADsReady]);
         // each warpgroup folds its RP/2 columns of the dR_k tile into registers
         if (graph) {
           if (!mbar_wait(&bars[kADrkFull], git & 1, abort_flag, 703)) {
@@ -556,8 +588,9 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
 // One CTA per (128-row query tile, head, sequence), looping over the causally
 // visible key tiles: S = Q K^T (+ R~_q R_k^T), dP = dO V^T (full 128x128 MMAs)
 // -> eight softmax-gradient warps (thread = query row = TMEM lane; warpgroup w
-// takes key columns [64w, 64w+64)) write dS as bf16 into the first half of
-// their own column range -> dQ += dS K, dR_q += dS R_k (TS form).
+// takes key columns [64w, 64w+64)) form P while the tensor core computes dP,
+// then write dS as bf16 into the first half of their own column range
+// -> dQ += dS K, dR_q += dS R_k (TS form).
 // TMEM columns: dQ [0,128) dR_q [128,128+r_pad) S [256,384) dP [384,512).
 template <int D, int RP>
 struct DqSmem {
@@ -585,9 +618,10 @@ enum DqBar {
   kBRqReady = 1,
   kBKvFull = 2,   // +stage
   kBKvEmpty = 4,  // +stage
-  kBStFull = 6,
+  kBSFull = 6,
   kBPReady = 7,
   kBAllDone = 8,
+  kBDPFull = 9,
 };
 
 constexpr int kDqThreads = 320;  // 8 softmax-gradient warps, producer, MMA
@@ -636,7 +670,8 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       mbar_init(&bars[kBKvFull + s], 1);
       mbar_init(&bars[kBKvEmpty + s], 1);
     }
-    mbar_init(&bars[kBStFull], 1);
+    mbar_init(&bars[kBSFull], 1);
+    mbar_init(&bars[kBDPFull], 1);
     mbar_init(&bars[kBPReady], 256);
     mbar_init(&bars[kBAllDone], 1);
     *abort_flag = 0;
@@ -713,13 +748,14 @@ __global__ void __launch_bounds__(kDqThreads, 1)
             mma_ss(tS, make_sdesc(sRq + kk * 32, 16, r_sbo, r_layout), make_sdesc(sRk + kk * 32, 16, r_sbo, r_layout),
                    idesc_s, 1);
         }
+        mma_commit(&bars[kBSFull]);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * L::kChunk + (kk & 3) * 32;
           mma_ss(tDP, make_sdesc(sDo + off, 16, 1024, kSwizzle128B), make_sdesc(sV + off, 16, 1024, kSwizzle128B),
                  idesc_s, kk > 0);
         }
-        mma_commit(&bars[kBStFull]);
+        mma_commit(&bars[kBDPFull]);
         if (!mbar_wait(&bars[kBPReady], j & 1, abort_flag, 904)) break;
         tc_fence_after();
 #pragma unroll
@@ -760,36 +796,44 @@ __global__ void __launch_bounds__(kDqThreads, 1)
     }
     const uint32_t tSw = tS + lane_base + 64 * wg, tDPw = tDP + lane_base + 64 * wg;
     for (int j = 0; ok && j < n_tiles; ++j) {
-      if (!mbar_wait(&bars[kBStFull], j & 1, abort_flag, 1002)) {
+      if (!mbar_wait(&bars[kBSFull], j & 1, abort_flag, 1002)) {
         ok = false;
         break;
       }
       tc_fence_after();
-#pragma unroll 1
+      // phase 1 (overlaps the dP MMA): P = exp2(S*c - LSE2) for this warp's 64 keys
+      float pf[64];
+#pragma unroll
       for (int c = 0; c < 2; ++c) {
-        uint32_t sv[32], dp[32];
+        uint32_t sv[32];
         tmem_ld32(tSw + 32 * c, sv);
-        tmem_ld32(tDPw + 32 * c, dp);
         tmem_ld_wait32(sv);
-        tmem_ld_wait32(dp);
         const int nvalid = limit - (j * kBlockN + 64 * wg + 32 * c);
-        uint32_t dd[16];
-        if (nvalid >= 32) {
+        if (nvalid < 32) {  // masked key columns get -inf exponents (ex2(-inf) = 0)
 #pragma unroll
-          for (int k = 0; k < 32; k += 2) {
-            const float p0 = ex2(fmaf(__uint_as_float(sv[k]), sl2, -lse2));
-            const float p1 = ex2(fmaf(__uint_as_float(sv[k + 1]), sl2, -lse2));
-            dd[k >> 1] = pack_bf16(p0 * (__uint_as_float(dp[k]) - delta), p1 * (__uint_as_float(dp[k + 1]) - delta));
-          }
-        } else {
-#pragma unroll
-          for (int k = 0; k < 32; k += 2) {
-            const float p0 = ex2(k < nvalid ? fmaf(__uint_as_float(sv[k]), sl2, -lse2) : -INFINITY);
-            const float p1 = ex2(k + 1 < nvalid ? fmaf(__uint_as_float(sv[k + 1]), sl2, -lse2) : -INFINITY);
-            dd[k >> 1] = pack_bf16(p0 * (__uint_as_float(dp[k]) - delta), p1 * (__uint_as_float(dp[k + 1]) - delta));
-          }
+          for (int k = 0; k < 32; ++k)
+            if (k >= nvalid) sv[k] = __float_as_uint(-INFINITY);
         }
-        tmem_st16(tSw + 16 * c, dd);  // columns this warp has already read
+#pragma unroll
+        for (int k = 0; k < 32; ++k) pf[32 * c + k] = ex2(fmaf(__uint_as_float(sv[k]), sl2, -lse2));
+      }
+      if (!mbar_wait(&bars[kBDPFull], j & 1, abort_flag, 1004)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      // phase 2: dS = P (dP - Delta), packed into columns this warp has already read
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t dp[32];
+        tmem_ld32(tDPw + 32 * c, dp);
+        tmem_ld_wait32(dp);
+        uint32_t dd[16];
+#pragma unroll
+        for (int k = 0; k < 32; k += 2)
+          dd[k >> 1] = pack_bf16(pf[32 * c + k] * (__uint_as_float(dp[k]) - delta),
+                                 pf[32 * c + k + 1] * (__uint_as_float(dp[k + 1]) - delta));
+        tmem_st16(tSw + 16 * c, dd);
       }
       tmem_st_wait();
       tc_fence_before();
