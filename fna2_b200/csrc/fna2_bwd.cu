@@ -319,6 +319,15 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
         const int s = it & 1;
         const int m0 = (m_start + mi) * kBlockM;
         float* lv = vec + s * 256;
+        // the row vectors do not depend on the TMA: fetch them (all at once) before waiting
+        float l2[4], dl[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int t = lane + 32 * u;
+          const bool valid = m0 + t < si.len_q;
+          l2[u] = valid ? __ldg(p.ws_lse2 + wbase + m0 + t) : 0.f;
+          dl[u] = valid ? __ldg(p.ws_delta + wbase + m0 + t) : 0.f;
+        }
         if (!mbar_wait(&bars[kAQFull + s], (it >> 1) & 1, abort_flag, 601)) {
           ok = false;
           break;
@@ -326,9 +335,8 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int t = lane + 32 * u;
-          const bool valid = m0 + t < si.len_q;
-          lv[t] = valid ? p.ws_lse2[wbase + m0 + t] : 0.f;
-          lv[128 + t] = valid ? p.ws_delta[wbase + m0 + t] : 0.f;
+          lv[t] = l2[u];
+          lv[128 + t] = dl[u];
           if (graph) scale_rows_inplace<RP>(smem + (s ? L::oRq1 : L::oRq0), t, f);
         }
         fence_proxy_async_smem();

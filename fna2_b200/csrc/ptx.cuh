@@ -66,11 +66,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Slow path of a bounded wait: spins on try_wait until the phase completes,
 // the CTA-wide abort flag is raised by another role, or kWaitTimeoutNs passes.
 // On timeout it raises the abort flag and records `site` in g_device_error.
+// The abort flag and the timer are checked once per 32 suspending try_waits,
+// so a phase that completes is noticed with the hardware's wake-up latency.
 __device__ __noinline__ static bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                                    int site) {
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
     if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
       *abort_flag = 1;
