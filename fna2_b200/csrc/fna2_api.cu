@@ -167,6 +167,16 @@ int map_qkv(CUtensorMap* m, const Fna2Tensor& t, const Shape& s, int rows, int h
   return make_map(m, t.ptr, s.D, rows, heads, s.batch_dim(), t.stride[2], t.stride[1], t.stride[0], 64, 128,
                   CU_TENSOR_MAP_SWIZZLE_128B, what);
 }
+// The key-stationary backward kernel tiles queries by 112 rows and reads R_q
+// as a third 64-column SW128 atom next to Q (columns past r zero-filled).
+int map_qkv112(CUtensorMap* m, const Fna2Tensor& t, const Shape& s, int rows, int heads, const char* what) {
+  return make_map(m, t.ptr, s.D, rows, heads, s.batch_dim(), t.stride[2], t.stride[1], t.stride[0], 64, kQT,
+                  CU_TENSOR_MAP_SWIZZLE_128B, what);
+}
+int map_r112(CUtensorMap* m, const Fna2Tensor& t, const Shape& s, int rows, const char* what) {
+  return make_map(m, t.ptr, s.r, rows, s.HG, s.batch_dim(), t.stride[2], t.stride[1], t.stride[0], 64, kQT,
+                  CU_TENSOR_MAP_SWIZZLE_128B, what);
+}
 int map_r(CUtensorMap* m, const Fna2Tensor& t, const Shape& s, int rows, const char* what) {
   return make_map(m, t.ptr, s.r, rows, s.HG, s.batch_dim(), t.stride[2], t.stride[1], t.stride[0], s.RP, 128,
                   s.RP == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B, what);
@@ -267,17 +277,21 @@ extern "C" int fna2_bwd(const Fna2BwdArgs* a, void* stream) {
     return fail(FNA2_ERR_WORKSPACE, "workspace too small: %zu < %zu bytes", a->workspace_bytes, need);
   FNA2_CHECK((reinterpret_cast<uintptr_t>(a->workspace) & 255u) == 0, "workspace must be 256-byte aligned");
 
-  CUtensorMap tq, tk, tv, tdo, trq, trk;
-  if (int rc = map_qkv(&tq, a->q, s, s.rows_q(), s.H, "q")) return rc;
-  if (int rc = map_qkv(&tk, a->k, s, s.rows_k(), s.HKV, "k")) return rc;
-  if (int rc = map_qkv(&tv, a->v, s, s.rows_k(), s.HKV, "v")) return rc;
-  if (int rc = map_qkv(&tdo, a->dout, s, s.rows_q(), s.H, "dout")) return rc;
+  BwdMaps m;
+  if (int rc = map_qkv(&m.q, a->q, s, s.rows_q(), s.H, "q")) return rc;
+  if (int rc = map_qkv(&m.k, a->k, s, s.rows_k(), s.HKV, "k")) return rc;
+  if (int rc = map_qkv(&m.v, a->v, s, s.rows_k(), s.HKV, "v")) return rc;
+  if (int rc = map_qkv(&m.dO, a->dout, s, s.rows_q(), s.H, "dout")) return rc;
+  if (int rc = map_qkv112(&m.q112, a->q, s, s.rows_q(), s.H, "q")) return rc;
+  if (int rc = map_qkv112(&m.dO112, a->dout, s, s.rows_q(), s.H, "dout")) return rc;
   if (s.HG > 0) {
-    if (int rc = map_r(&trq, a->r_q, s, s.rows_q(), "r_q")) return rc;
-    if (int rc = map_r(&trk, a->r_k, s, s.rows_k(), "r_k")) return rc;
+    if (int rc = map_r(&m.rq, a->r_q, s, s.rows_q(), "r_q")) return rc;
+    if (int rc = map_r(&m.rk, a->r_k, s, s.rows_k(), "r_k")) return rc;
+    if (int rc = map_r112(&m.rq112, a->r_q, s, s.rows_q(), "r_q")) return rc;
   } else {
-    trq = tq;
-    trk = tk;
+    m.rq = m.q;  // never dereferenced: no graph heads
+    m.rk = m.k;
+    m.rq112 = m.q112;
   }
   BwdParams p;
   std::memset(&p, 0, sizeof(p));
@@ -315,7 +329,7 @@ extern "C" int fna2_bwd(const Fna2BwdArgs* a, void* stream) {
   p.n_mblocks = (s.Sq + kBlockM - 1) / kBlockM;
   p.n_nblocks = (s.Sk + kBlockN - 1) / kBlockN;
   bwd_set_workspace(&p, a->workspace, s.batch_dim(), s.H, s.rows_q());
-  FNA2_CUDA(launch_bwd(s.D, s.RP, tq, tk, tv, tdo, trq, trk, p, static_cast<cudaStream_t>(stream),
+  FNA2_CUDA(launch_bwd(s.D, s.RP, m, p, static_cast<cudaStream_t>(stream),
                        reinterpret_cast<cudaEvent_t*>(a->launch_events)));
   return FNA2_OK;
 }

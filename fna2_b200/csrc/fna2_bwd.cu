@@ -139,34 +139,44 @@ __device__ __forceinline__ uint32_t r_layout_of(int rp) {
 // ---------------------------------------------------------------------------
 // dK / dV / dR_k  (KV-stationary)
 // ---------------------------------------------------------------------------
-// Per query tile: S^T = K Q^T (+ R_k R~_q^T) and dP^T = V dO^T as full 128x128
-// MMAs; eight softmax-gradient warps (two warpgroups; thread = key row = TMEM
-// lane) each take 64 of the 128 query columns and write P^T and dS^T back as
-// bf16 into the first half of their OWN column range (so no warp overwrites
-// columns another warp still has to read).  The hand-offs are split so the
-// phases overlap: the warps form P^T while the tensor core computes dP^T, and
-// dV += P^T dO runs while they form dS^T; then dK += dS^T Q and the dR_k tile
-// dS^T R~_q (TS-form MMAs reading P^T / dS^T from TMEM).
-// TMEM columns: dV [0,128) dK [128,256) S^T [256,384) dP^T [384,512).
-// P^T of query columns [64w, 64w+64) sits at S^T columns [64w, 64w+32), dS^T
-// likewise in dP^T; the dR_k tile uses dP^T columns [32, 32+r_pad), which
-// warpgroup 0 folds into registers before the next dP^T overwrites them.
+// One CTA per (128-row key tile, KV head, sequence), looping over the query
+// heads of the GQA group and the causally visible 112-row query tiles.
+//
+// The bias enters the score MMA as R~_k R_q^T with R~_k = R_k*gs/scale, scaled
+// in shared memory once per head.  dR_k rides along with dK as extra
+// accumulator columns: the B operand of the dK MMA is [Q | R_q] (R_q stored as
+// a zero-padded third 64-column swizzle atom next to Q's two), so one
+// N = D + r_pad MMA per k-step yields dK and dS^T R_q (dR_k = gs * that).  112-row query tiles are what make the extra
+// columns fit in TMEM:
+//   dV [0,128) | dK,dR_k [128,288) | S^T [288,400) | dP^T [400,512)
+// Per query tile (112 columns; warpgroup 0 owns columns [0,64), warpgroup 1
+// [64,112), each thread one key row = TMEM lane):
+//   tensor core:  S^T = K Q^T (+ R~_k R_q^T), dP^T = V dO^T  (SS)
+//   warps:        P^T = exp2(S^T*c - LSE2) -> bf16 into the first half of each
+//                 warpgroup's own S^T columns; dS^T = P^T (dP^T - Delta)
+//                 likewise into dP^T
+//   tensor core:  dV += P^T dO, [dK | dR_k] += dS^T [Q | R_q]  (TS form)
+// The MMA stream runs the next tile's S^T (its stage was loaded a tile ahead)
+// while the warps form dS^T, and dK plus the next dP^T while they form the next
+// P^T.
+constexpr int kQT = 112;  // query rows per backward (dK/dV) tile
+
 template <int D, int RP>
 struct DkdvSmem {
-  static constexpr int kTile = 128 * D * 2;
-  static constexpr int kR = 128 * RP * 2;
-  static constexpr int kChunk = 128 * 128;
+  static constexpr int kKTile = 128 * D * 2;
+  static constexpr int kKChunk = 128 * 128;
+  static constexpr int kQChunk = kQT * 128;            // one 64-column swizzle atom of a 112-row tile
+  static constexpr int kQAtoms = D / 64 + 1;           // Q chunks + the padded R~_q atom
+  static constexpr int kRk = 128 * RP * 2;
   static constexpr int align(int x) { return (x + 1023) & ~1023; }
   static constexpr int oK = 0;
-  static constexpr int oV = align(oK + kTile);
-  static constexpr int oRk = align(oV + kTile);
-  static constexpr int oQ0 = align(oRk + kR);
-  static constexpr int oQ1 = align(oQ0 + kTile);
-  static constexpr int oDo0 = align(oQ1 + kTile);
-  static constexpr int oDo1 = align(oDo0 + kTile);
-  static constexpr int oRq0 = align(oDo1 + kTile);
-  static constexpr int oRq1 = align(oRq0 + kR);
-  static constexpr int oVec = align(oRq1 + kR);  // [2 stages][lse2 128 | delta 128] floats
+  static constexpr int oV = align(oK + kKTile);
+  static constexpr int oRk = align(oV + kKTile);
+  static constexpr int oQ0 = align(oRk + kRk);                 // [Q c0 | (Q c1) | R~_q] per stage
+  static constexpr int oQ1 = align(oQ0 + kQAtoms * kQChunk);
+  static constexpr int oDo0 = align(oQ1 + kQAtoms * kQChunk);
+  static constexpr int oDo1 = align(oDo0 + (D / 64) * kQChunk);
+  static constexpr int oVec = align(oDo1 + (D / 64) * kQChunk);  // [2 stages][lse2 128 | delta 128] floats
   static constexpr int oBar = oVec + 2 * 256 * 4;
   static constexpr int kNumBars = 20;
   static constexpr int oMisc = oBar + kNumBars * 8;
@@ -181,15 +191,47 @@ enum DkdvBar {
   kAQEmpty = 5,   // +stage
   kAPrep = 7,     // +stage
   kASFull = 9,
-  kAPReady = 10,
-  kADrkFull = 11,
-  kADrkFree = 12,
-  kAAllDone = 13,
-  kADPFull = 14,
-  kADsReady = 15,
+  kADPFull = 10,
+  kAPReady = 11,
+  kADsReady = 12,
+  kAHeadDone = 13,
+  kAAllDone = 14,
+  kARkReady = 15,  // R~_k scaled in shared memory (once per graph head)
 };
 
 constexpr int kDkdvThreads = 352;  // 8 softmax-gradient warps, producer, MMA, prep
+
+// P^T for one chunk of up to 32 query columns [qb, qb+ncol) of one key row:
+// exp2(S^T*c - LSE2), packed into pk[o .. o+16).  Columns outside [q_lo, q_hi)
+// (causal, sequence end) and past ncol get exactly 0.
+__device__ __forceinline__ void p_chunk_bwd(uint32_t (&sv)[32], uint32_t (&pk)[32], const int o, const int qb,
+                                            const int ncol, const int q_lo, const int q_hi, const float* lv,
+                                            const float sl2) {
+  if (ncol == 32 && qb >= q_lo && qb + 32 <= q_hi) {
+#pragma unroll
+    for (int k = 0; k < 32; k += 4) {
+      const float4 l4 = *reinterpret_cast<const float4*>(&lv[qb + k]);
+      pk[o + (k >> 1)] = pack_bf16(ex2(fmaf(__uint_as_float(sv[k]), sl2, -l4.x)),
+                                   ex2(fmaf(__uint_as_float(sv[k + 1]), sl2, -l4.y)));
+      pk[o + (k >> 1) + 1] = pack_bf16(ex2(fmaf(__uint_as_float(sv[k + 2]), sl2, -l4.z)),
+                                       ex2(fmaf(__uint_as_float(sv[k + 3]), sl2, -l4.w)));
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {  // masked columns: -inf exponent, ex2(-inf) = 0
+      const int qi = qb + k;
+      if (!(k < ncol && qi >= q_lo && qi < q_hi)) sv[k] = __float_as_uint(-INFINITY);
+    }
+#pragma unroll
+    for (int k = 0; k < 32; k += 4) {
+      const float4 l4 = *reinterpret_cast<const float4*>(&lv[qb + k]);
+      pk[o + (k >> 1)] = pack_bf16(ex2(fmaf(__uint_as_float(sv[k]), sl2, -l4.x)),
+                                   ex2(fmaf(__uint_as_float(sv[k + 1]), sl2, -l4.y)));
+      pk[o + (k >> 1) + 1] = pack_bf16(ex2(fmaf(__uint_as_float(sv[k + 2]), sl2, -l4.z)),
+                                       ex2(fmaf(__uint_as_float(sv[k + 3]), sl2, -l4.w)));
+    }
+  }
+}
 
 template <int D, int RP>
 __global__ void __launch_bounds__(kDkdvThreads, 1)
@@ -213,8 +255,9 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
   if (n0 >= si.len_k) return;
   const int g = P.heads / P.heads_kv;
   const int gh = max(0, min(g, P.heads_graph - hk * g));  // graph heads of this group (a prefix)
-  const int m_start = P.causal ? n_blk : 0;
-  const int m_end = (si.len_q + kBlockM - 1) / kBlockM;
+  // causal: query tile m sees key rows [n0, n0+128) iff 112*m + 111 >= n0
+  const int m_start = P.causal ? n0 / kQT : 0;
+  const int m_end = (si.len_q + kQT - 1) / kQT;
   const int n_it = max(0, m_end - m_start);
   const int total_it = g * n_it;
   const int warp = warp_id();
@@ -247,9 +290,9 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
     mbar_init(&bars[kADPFull], 1);
     mbar_init(&bars[kAPReady], 256);
     mbar_init(&bars[kADsReady], 256);
-    mbar_init(&bars[kADrkFull], 1);
-    mbar_init(&bars[kADrkFree], 256);
+    mbar_init(&bars[kAHeadDone], 1);
     mbar_init(&bars[kAAllDone], 1);
+    mbar_init(&bars[kARkReady], 32);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -261,9 +304,10 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tDV = tmem + 0, tDK = tmem + 128, tS = tmem + 256, tDP = tmem + 384, tDRK = tmem + 384 + 32;
+  const uint32_t tDV = tmem + 0, tDK = tmem + 128, tS = tmem + 288, tDP = tmem + 400;
   // TMEM column of the packed bf16 operand for the 16 query rows of k-step kk
   auto packed_col = [](int kk) { return (kk < 4 ? 0 : 64) + (kk & 3) * 8; };
+  auto graph_of = [&](int it) { return it / n_it < gh; };
 
   if (warp == 8) {
     // ------------------------------------------------------------ producer
@@ -271,11 +315,11 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmDo);
       const int krow = si.k_start + n0;
-      mbar_expect_tx(&bars[kAKV], 2 * L::kTile);
+      mbar_expect_tx(&bars[kAKV], 2 * L::kKTile);
 #pragma unroll
       for (int c = 0; c < D / 64; ++c) {
-        tma_load_4d(smem + L::oK + c * L::kChunk, &tmK, &bars[kAKV], c * 64, krow, hk, si.b);
-        tma_load_4d(smem + L::oV + c * L::kChunk, &tmV, &bars[kAKV], c * 64, krow, hk, si.b);
+        tma_load_4d(smem + L::oK + c * L::kKChunk, &tmK, &bars[kAKV], c * 64, krow, hk, si.b);
+        tma_load_4d(smem + L::oV + c * L::kKChunk, &tmV, &bars[kAKV], c * 64, krow, hk, si.b);
       }
       int it = 0;
       bool ok = true;
@@ -284,7 +328,7 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
         const bool graph = e < gh;
         if (graph) {
           if (e > 0 && !mbar_wait(&bars[kARkEmpty], (e - 1) & 1, abort_flag, 401)) break;
-          mbar_expect_tx(&bars[kARkFull], L::kR);
+          mbar_expect_tx(&bars[kARkFull], L::kRk);
           tma_load_4d(smem + L::oRk, &tmRk, &bars[kARkFull], 0, krow, h, si.b);
         }
         for (int mi = 0; mi < n_it; ++mi, ++it) {
@@ -293,147 +337,154 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
             ok = false;
             break;
           }
-          const int qrow = si.q_start + (m_start + mi) * kBlockM;
-          mbar_expect_tx(&bars[kAQFull + s], 2 * L::kTile + (graph ? L::kR : 0));
+          const int qrow = si.q_start + (m_start + mi) * kQT;
+          uint8_t* sq = smem + (s ? L::oQ1 : L::oQ0);
+          uint8_t* sdo = smem + (s ? L::oDo1 : L::oDo0);
+          mbar_expect_tx(&bars[kAQFull + s], 2 * (D / 64) * L::kQChunk + (graph ? L::kQChunk : 0));
 #pragma unroll
           for (int c = 0; c < D / 64; ++c) {
-            tma_load_4d(smem + (s ? L::oQ1 : L::oQ0) + c * L::kChunk, &tmQ, &bars[kAQFull + s], c * 64, qrow, h,
-                        si.b);
-            tma_load_4d(smem + (s ? L::oDo1 : L::oDo0) + c * L::kChunk, &tmDo, &bars[kAQFull + s], c * 64, qrow,
-                        h, si.b);
+            tma_load_4d(sq + c * L::kQChunk, &tmQ, &bars[kAQFull + s], c * 64, qrow, h, si.b);
+            tma_load_4d(sdo + c * L::kQChunk, &tmDo, &bars[kAQFull + s], c * 64, qrow, h, si.b);
           }
-          if (graph) tma_load_4d(smem + (s ? L::oRq1 : L::oRq0), &tmRq, &bars[kAQFull + s], 0, qrow, h, si.b);
+          if (graph) tma_load_4d(sq + (D / 64) * L::kQChunk, &tmRq, &bars[kAQFull + s], 0, qrow, h, si.b);
         }
       }
     }
   } else if (warp == 10) {
-    // ------------------------------------------------------------ prep: lse2/Delta rows, R~_q
-    int it = 0;
-    bool ok = true;
-    for (int e = 0; ok && e < g; ++e) {
-      const int h = hk * g + e;
-      const bool graph = e < gh;
-      const float f = graph ? __ldg(P.gs + h) / scale : 0.f;
-      const int64_t wbase = (static_cast<int64_t>(si.b) * P.heads + h) * p.ws_sbh + si.q_start;
-      for (int mi = 0; mi < n_it; ++mi, ++it) {
-        const int s = it & 1;
-        const int m0 = (m_start + mi) * kBlockM;
-        float* lv = vec + s * 256;
-        // the row vectors do not depend on the TMA: fetch them (all at once) before waiting
-        float l2[4], dl[4];
+    // ------------------------------------------------------------ prep: lse2/Delta rows, R~_k
+    // the row vectors of tile it+1 are fetched while tile it is staged
+    auto fetch = [&](int it, float (&l2)[4], float (&dl)[4]) {
+      const int e = it / n_it, mi = it % n_it;
+      const int64_t wbase = (static_cast<int64_t>(si.b) * P.heads + hk * g + e) * p.ws_sbh + si.q_start;
+      const int m0 = (m_start + mi) * kQT;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int t = lane + 32 * u;
-          const bool valid = m0 + t < si.len_q;
-          l2[u] = valid ? __ldg(p.ws_lse2 + wbase + m0 + t) : 0.f;
-          dl[u] = valid ? __ldg(p.ws_delta + wbase + m0 + t) : 0.f;
-        }
-        if (!mbar_wait(&bars[kAQFull + s], (it >> 1) & 1, abort_flag, 601)) {
+      for (int u = 0; u < 4; ++u) {
+        const int t = lane + 32 * u;
+        const bool valid = t < kQT && m0 + t < si.len_q;
+        l2[u] = valid ? __ldg(p.ws_lse2 + wbase + m0 + t) : 0.f;
+        dl[u] = valid ? __ldg(p.ws_delta + wbase + m0 + t) : 0.f;
+      }
+    };
+    float l2[4], dl[4], nl2[4], ndl[4];
+    fetch(0, l2, dl);
+    bool ok = true;
+    for (int it = 0; ok && it < total_it; ++it) {
+      const int s = it & 1;
+      const int e = it / n_it;
+      if (e < gh && (it % n_it) == 0) {
+        // a new graph head: R~_k = R_k * gs/scale in place (element-wise, any swizzle)
+        if (!mbar_wait(&bars[kARkFull], e & 1, abort_flag, 602)) {
           ok = false;
           break;
         }
+        const float f = __ldg(P.gs + hk * g + e) / scale;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int t = lane + 32 * u;
-          lv[t] = l2[u];
-          lv[128 + t] = dl[u];
-          if (graph) scale_rows_inplace<RP>(smem + (s ? L::oRq1 : L::oRq0), t, f);
-        }
+        for (int u = 0; u < 4; ++u) scale_rows_inplace<RP>(smem + L::oRk, lane + 32 * u, f);
         fence_proxy_async_smem();
-        mbar_arrive(&bars[kAPrep + s]);
+        mbar_arrive(&bars[kARkReady]);
+      }
+      if (it + 1 < total_it) fetch(it + 1, nl2, ndl);
+      if (!mbar_wait(&bars[kAQFull + s], (it >> 1) & 1, abort_flag, 601)) {
+        ok = false;
+        break;
+      }
+      float* lv = vec + s * 256;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        lv[lane + 32 * u] = l2[u];
+        lv[128 + lane + 32 * u] = dl[u];
+      }
+      mbar_arrive(&bars[kAPrep + s]);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        l2[u] = nl2[u];
+        dl[u] = ndl[u];
       }
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_st = make_idesc_bf16(128, 128, 0, 0);   // S^T, dP^T
-      constexpr uint32_t idesc_acc = make_idesc_bf16(128, D, 0, 1);    // dV, dK (A in TMEM, B MN-major)
-      constexpr uint32_t idesc_drk = make_idesc_bf16(128, RP, 0, 1);   // dR_k tile
+      constexpr uint32_t idesc_st = make_idesc_bf16(128, kQT, 0, 0);      // S^T, dP^T (N = 112 queries)
+      constexpr uint32_t idesc_dv = make_idesc_bf16(128, D, 0, 1);        // dV (A in TMEM, B MN-major)
+      constexpr uint32_t idesc_dk = make_idesc_bf16(128, D, 0, 1);        // dK only (vanilla heads)
+      constexpr uint32_t idesc_dkr = make_idesc_bf16(128, D + RP, 0, 1);  // [dK | dR_k]
       const uint32_t r_layout = r_layout_of(RP);
       const uint32_t r_sbo = 8 * RP * 2;
       const uint32_t sK = smem_u32(smem + L::oK), sV = smem_u32(smem + L::oV), sRk = smem_u32(smem + L::oRk);
-      auto graph_of = [&](int it) { return it / n_it < gh; };
-      bool ok = mbar_wait(&bars[kAKV], 0, abort_flag, 501);
-      int git = 0;
-      for (int it = 0; ok && it < total_it; ++it) {
+      auto stage_q = [&](int it) { return smem_u32(smem + ((it & 1) ? L::oQ1 : L::oQ0)); };
+      auto stage_do = [&](int it) { return smem_u32(smem + ((it & 1) ? L::oDo1 : L::oDo0)); };
+      auto wait_stage = [&](int it) -> bool {
         const int s = it & 1;
-        const bool graph = graph_of(it);
-        const bool first_of_head = (it % n_it) == 0, last_of_head = (it % n_it) == n_it - 1;
-        const uint32_t sQ = smem_u32(smem + (s ? L::oQ1 : L::oQ0));
-        const uint32_t sDo = smem_u32(smem + (s ? L::oDo1 : L::oDo0));
-        const uint32_t sRq = smem_u32(smem + (s ? L::oRq1 : L::oRq0));
-        if (!mbar_wait(&bars[kAQFull + s], (it >> 1) & 1, abort_flag, 503) ||
-            !mbar_wait(&bars[kAPrep + s], (it >> 1) & 1, abort_flag, 504) ||
-            (graph && first_of_head && !mbar_wait(&bars[kARkFull], (it / n_it) & 1, abort_flag, 502))) {
-          ok = false;
-          break;
-        }
+        if (!mbar_wait(&bars[kAQFull + s], (it >> 1) & 1, abort_flag, 503)) return false;
+        if (!mbar_wait(&bars[kAPrep + s], (it >> 1) & 1, abort_flag, 504)) return false;
+        if (graph_of(it) && (it % n_it) == 0 && !mbar_wait(&bars[kARkReady], (it / n_it) & 1, abort_flag, 502))
+          return false;
         tc_fence_after();
-        // S^T = K Q^T (+ R_k R~_q^T)
+        return true;
+      };
+      auto issue_s = [&](int it) {  // S^T = K Q^T (+ R~_k R_q^T)
+        const uint32_t sQ = stage_q(it);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * L::kChunk + (kk & 3) * 32;
-          mma_ss(tS, make_sdesc(sK + off, 16, 1024, kSwizzle128B), make_sdesc(sQ + off, 16, 1024, kSwizzle128B),
-                 idesc_st, kk > 0);
-        }
-        if (graph) {
+        for (int kk = 0; kk < D / 16; ++kk)
+          mma_ss(tS, make_sdesc(sK + (kk >> 2) * L::kKChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B),
+                 make_sdesc(sQ + (kk >> 2) * L::kQChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B), idesc_st, kk > 0);
+        if (graph_of(it)) {
+          const uint32_t sRq = sQ + (D / 64) * L::kQChunk;
 #pragma unroll
           for (int kk = 0; kk < RP / 16; ++kk)
-            mma_ss(tS, make_sdesc(sRk + kk * 32, 16, r_sbo, r_layout), make_sdesc(sRq + kk * 32, 16, r_sbo, r_layout),
+            mma_ss(tS, make_sdesc(sRk + kk * 32, 16, r_sbo, r_layout), make_sdesc(sRq + kk * 32, 16, 1024, kSwizzle128B),
                    idesc_st, 1);
-          if (last_of_head) mma_commit(&bars[kARkEmpty]);
+          if ((it % n_it) == n_it - 1) mma_commit(&bars[kARkEmpty]);  // last use of this head's R_k
         }
         mma_commit(&bars[kASFull]);
-        // dP^T = V dO^T overwrites the previous dR_k tile: wait until it was folded
-        if (it > 0 && !mbar_wait(&bars[kADrkFree], (it - 1) & 1, abort_flag, 505)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+      };
+      auto issue_dp = [&](int it) {  // dP^T = V dO^T
+        const uint32_t sDo = stage_do(it);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * L::kChunk + (kk & 3) * 32;
-          mma_ss(tDP, make_sdesc(sV + off, 16, 1024, kSwizzle128B), make_sdesc(sDo + off, 16, 1024, kSwizzle128B),
-                 idesc_st, kk > 0);
-        }
+        for (int kk = 0; kk < D / 16; ++kk)
+          mma_ss(tDP, make_sdesc(sV + (kk >> 2) * L::kKChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B),
+                 make_sdesc(sDo + (kk >> 2) * L::kQChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B), idesc_st, kk > 0);
         mma_commit(&bars[kADPFull]);
-        if (!mbar_wait(&bars[kAPReady], it & 1, abort_flag, 506)) {
-          ok = false;
-          break;
-        }
+      };
+
+      bool ok = mbar_wait(&bars[kAKV], 0, abort_flag, 501) && wait_stage(0);
+      if (ok) {
+        issue_s(0);
+        issue_dp(0);
+      }
+      for (int it = 0; ok && it < total_it; ++it) {
+        const bool graph = graph_of(it);
+        // dV += P^T dO   (K = 112 query rows, 7 steps of 16)
+        if (!mbar_wait(&bars[kAPReady], it & 1, abort_flag, 506)) break;
         tc_fence_after();
-        // dV += P^T dO   (K = 128 query rows, 8 steps of 16)
+        const uint32_t sDo = stage_do(it), sQ = stage_q(it);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_ts(tDV, tS + packed_col(kk), make_sdesc(sDo + kk * 2048, L::kChunk, 1024, kSwizzle128B), idesc_acc,
+        for (int kk = 0; kk < kQT / 16; ++kk)
+          mma_ts(tDV, tS + packed_col(kk), make_sdesc(sDo + kk * 2048, L::kQChunk, 1024, kSwizzle128B), idesc_dv,
                  (it > 0 || kk > 0) ? 1u : 0u);
-        if (!mbar_wait(&bars[kADsReady], it & 1, abort_flag, 507)) {
-          ok = false;
-          break;
+        // next tile's S^T overlaps the warps' dS^T work (P^T above was read in order;
+        // the stage was loaded while the previous tile ran)
+        if (it + 1 < total_it) {
+          if (!wait_stage(it + 1)) break;
+          issue_s(it + 1);
         }
+        // [dK | dR_k] += dS^T [Q | R_q]
+        if (!mbar_wait(&bars[kADsReady], it & 1, abort_flag, 507)) break;
         tc_fence_after();
-        // dK += dS^T Q
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_ts(tDK, tDP + packed_col(kk), make_sdesc(sQ + kk * 2048, L::kChunk, 1024, kSwizzle128B), idesc_acc,
-                 (it > 0 || kk > 0) ? 1u : 0u);
-        if (graph) {
-          // dR_k tile = dS^T R~_q  (B MN-major: r_pad contiguous, rows of RP*2 bytes)
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            mma_ts(tDRK, tDP + packed_col(kk), make_sdesc(sRq + kk * 16 * RP * 2, 16, r_sbo, r_layout), idesc_drk,
-                   kk > 0 ? 1u : 0u);
-          mma_commit(&bars[kADrkFull]);
-          ++git;
-        }
-        mma_commit(&bars[kAQEmpty + s]);
+        for (int kk = 0; kk < kQT / 16; ++kk)
+          mma_ts(tDK, tDP + packed_col(kk), make_sdesc(sQ + kk * 2048, L::kQChunk, 1024, kSwizzle128B),
+                 graph ? idesc_dkr : idesc_dk, (it > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&bars[kAQEmpty + (it & 1)]);
+        if (graph && (it % n_it) == n_it - 1 && it + 1 < total_it) mma_commit(&bars[kAHeadDone]);
+        // next tile's dP^T overlaps the warps' next P^T work (dS^T above was read in order)
+        if (it + 1 < total_it) issue_dp(it + 1);
       }
       if (ok) mma_commit(&bars[kAAllDone]);
     }
   } else {
     // ------------------------------------------------------------ softmax-gradient warps 0-7
-    const int wg = warp >> 2;  // warpgroup: query columns [64*wg, 64*wg+64) of every tile
-    const int hh = wg;         // epilogue: D-column half stored by this warpgroup
+    const int wg = warp >> 2;  // warpgroup: query columns [64*wg, min(64*wg+64, 112))
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int t = tid & 127;   // key row within the tile (TMEM lane)
     const int kv_local = n0 + t;
@@ -441,20 +492,22 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
     const float sl2 = P.scale_log2;
     const int64_t krow = si.k_start + kv_local;
     const uint32_t tSw = tS + lane_base + 64 * wg, tDPw = tDP + lane_base + 64 * wg;
-    float drk_acc[RP / 2];  // this warpgroup's dR_k columns [wg*RP/2, (wg+1)*RP/2)
+    constexpr int kW1 = kQT - 64;  // columns owned by warpgroup 1
+    float drk_prev[RP];                       // dR_k columns already stored for earlier heads
 #pragma unroll
-    for (int i = 0; i < RP / 2; ++i) drk_acc[i] = 0.f;
-    int it = 0, git = 0;
+    for (int i = 0; i < RP; ++i) drk_prev[i] = 0.f;
+    int it = 0, hb = 0;
     bool ok = true;
+
     for (int e = 0; ok && e < g; ++e) {
       const int h = hk * g + e;
       const bool graph = e < gh;
       for (int mi = 0; mi < n_it; ++mi, ++it) {
         const int s = it & 1;
-        const int m0 = (m_start + mi) * kBlockM;
+        const int m0 = (m_start + mi) * kQT;
         const float* lv = vec + s * 256;
         // valid query columns q in [q_lo, q_hi) (tile-relative) for this key row
-        const int q_hi = kv_valid ? (si.len_q - m0) : 0;
+        const int q_hi = kv_valid ? min(kQT, si.len_q - m0) : 0;
         const int q_lo = P.causal ? (kv_local - m0) : 0;
         if (!mbar_wait(&bars[kAPrep + s], (it >> 1) & 1, abort_flag, 702) ||
             !mbar_wait(&bars[kASFull], it & 1, abort_flag, 701)) {
@@ -462,122 +515,150 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
           break;
         }
         tc_fence_after();
-        // phase 1 (overlaps the dP^T MMA): P^T = exp2(S^T*c - LSE2) in two
-        // 32-column chunks; chunk c's packed output lands in columns
-        // [16c, 16c+16) of this warp's range, which it has already read
-        uint32_t pk[32];  // P as packed bf16 pairs, kept for phase 2
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
+        // phase 1: P^T (packed bf16, kept in registers for phase 2)
+        uint32_t pk[32];
+        {
           uint32_t sv[32];
-          tmem_ld32(tSw + 32 * c, sv);
+          tmem_ld32(tSw, sv);
           tmem_ld_wait32(sv);
-          const int qb = 64 * wg + 32 * c;
-          if (!((qb >= q_lo) && (qb + 32 <= q_hi))) {  // masked columns: -inf exponent
-#pragma unroll
-            for (int k = 0; k < 32; ++k) {
-              const int qi = qb + k;
-              if (!(qi >= q_lo && qi < q_hi)) sv[k] = __float_as_uint(-INFINITY);
-            }
+          p_chunk_bwd(sv, pk, 0, 64 * wg, 32, q_lo, q_hi, lv, sl2);
+          if (wg == 0) {
+            tmem_ld32(tSw + 32, sv);
+            tmem_ld_wait32(sv);
+            p_chunk_bwd(sv, pk, 16, 32, 32, q_lo, q_hi, lv, sl2);
+          } else {
+            tmem_ld16(tSw + 32, sv);
+            tmem_ld_wait16(sv);
+            p_chunk_bwd(sv, pk, 16, 96, kW1 - 32, q_lo, q_hi, lv, sl2);
           }
-#pragma unroll
-          for (int k = 0; k < 32; k += 4) {
-            const float4 l4 = *reinterpret_cast<const float4*>(&lv[qb + k]);
-            const float p0 = ex2(fmaf(__uint_as_float(sv[k]), sl2, -l4.x));
-            const float p1 = ex2(fmaf(__uint_as_float(sv[k + 1]), sl2, -l4.y));
-            const float p2 = ex2(fmaf(__uint_as_float(sv[k + 2]), sl2, -l4.z));
-            const float p3 = ex2(fmaf(__uint_as_float(sv[k + 3]), sl2, -l4.w));
-            pk[16 * c + (k >> 1)] = pack_bf16(p0, p1);
-            pk[16 * c + (k >> 1) + 1] = pack_bf16(p2, p3);
-          }
-          tmem_st16(tSw + 16 * c, pk + 16 * c);
         }
+        tmem_st32(tSw, pk);  // columns this warpgroup has already read (16 unused by warpgroup 1)
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&bars[kAPReady]);
-        // phase 2 (overlaps the dV MMA): dS^T = P^T (dP^T - Delta), with the
-        // same bf16-rounded P that the dV MMA consumes
+        // phase 2: dS^T = P^T (dP^T - Delta)
         if (!mbar_wait(&bars[kADPFull], it & 1, abort_flag, 704)) {
           ok = false;
           break;
         }
         tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t dp[32];
-          tmem_ld32(tDPw + 32 * c, dp);
+        {
+          uint32_t dp[32], dd[32];
+          tmem_ld32(tDPw, dp);
           tmem_ld_wait32(dp);
-          const int qb = 64 * wg + 32 * c;
-          uint32_t dd[16];
 #pragma unroll
           for (int k = 0; k < 32; k += 4) {
-            const float4 d4 = *reinterpret_cast<const float4*>(&lv[128 + qb + k]);
-            const uint32_t a = pk[16 * c + (k >> 1)], b = pk[16 * c + (k >> 1) + 1];
+            const float4 d4 = *reinterpret_cast<const float4*>(&lv[128 + 64 * wg + k]);
+            const uint32_t a = pk[k >> 1], b = pk[(k >> 1) + 1];
             dd[k >> 1] = pack_bf16(__uint_as_float(a << 16) * (__uint_as_float(dp[k]) - d4.x),
                                    __uint_as_float(a & 0xffff0000u) * (__uint_as_float(dp[k + 1]) - d4.y));
             dd[(k >> 1) + 1] = pack_bf16(__uint_as_float(b << 16) * (__uint_as_float(dp[k + 2]) - d4.z),
                                          __uint_as_float(b & 0xffff0000u) * (__uint_as_float(dp[k + 3]) - d4.w));
           }
-          tmem_st16(tDPw + 16 * c, dd);
+          if (wg == 0) {
+            tmem_ld32(tDPw + 32, dp);
+            tmem_ld_wait32(dp);
+          } else {
+            tmem_ld16(tDPw + 32, dp);
+            tmem_ld_wait16(dp);
+#pragma unroll
+            for (int k = 16; k < 32; ++k) dp[k] = 0u;  // beyond the 112-column tile
+          }
+#pragma unroll
+          for (int k = 0; k < 32; k += 4) {
+            const float4 d4 = *reinterpret_cast<const float4*>(&lv[128 + 64 * wg + 32 + k]);
+            const uint32_t a = pk[16 + (k >> 1)], b = pk[16 + (k >> 1) + 1];
+            dd[16 + (k >> 1)] = pack_bf16(__uint_as_float(a << 16) * (__uint_as_float(dp[k]) - d4.x),
+                                          __uint_as_float(a & 0xffff0000u) * (__uint_as_float(dp[k + 1]) - d4.y));
+            dd[16 + (k >> 1) + 1] = pack_bf16(__uint_as_float(b << 16) * (__uint_as_float(dp[k + 2]) - d4.z),
+                                              __uint_as_float(b & 0xffff0000u) * (__uint_as_float(dp[k + 3]) - d4.w));
+          }
+          tmem_st32(tDPw, dd);
         }
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&bars[kADsReady]);
-        // each warpgroup folds its RP/2 columns of the dR_k tile into registers
-        if (graph) {
-          if (!mbar_wait(&bars[kADrkFull], git & 1, abort_flag, 703)) {
+        // GQA: at the end of a graph head that is followed by another head, store
+        // this head's dR_k columns (accumulated on top of the earlier heads')
+        if (wg == 0 && graph && mi == n_it - 1 && it + 1 < total_it) {
+          if (!mbar_wait(&bars[kAHeadDone], hb & 1, abort_flag, 705)) {
             ok = false;
             break;
           }
-          ++git;
+          ++hb;
           tc_fence_after();
-          uint32_t rv[16];
+          const float gsh = __ldg(P.gs + h);  // dR_k = gs * dS^T R_q
+          uint32_t rv[32];
           if (RP == 16) {
-            tmem_ld8(tDRK + lane_base + 8 * wg, rv);
-            tmem_ld_wait8(rv);
-          } else {
-            tmem_ld16(tDRK + lane_base + 16 * wg, rv);
+            tmem_ld16(tDK + lane_base + D, rv);
             tmem_ld_wait16(rv);
+          } else {
+            tmem_ld32(tDK + lane_base + D, rv);
+            tmem_ld_wait32(rv);
           }
-#pragma unroll
-          for (int i = 0; i < RP / 2; ++i) drk_acc[i] += __uint_as_float(rv[i]);
-        }
-        tc_fence_before();
-        mbar_arrive(&bars[kADrkFree]);
-        if (graph && mi == n_it - 1) {
           if (kv_valid) {
-            __nv_bfloat16* dst = p.drk + si.b * p.drk_sb + h * p.drk_sh + krow * p.drk_sr + wg * (RP / 2);
+            __nv_bfloat16* dst = p.drk + si.b * p.drk_sb + h * p.drk_sh + krow * p.drk_sr;
 #pragma unroll
-            for (int c = 0; c < RP / 2; c += 8) {
-              if (wg * (RP / 2) + c < P.rank) {
+            for (int c = 0; c < RP; c += 8) {
+              if (c < P.rank) {
                 uint4 w;
                 uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
-                  wp[i] = pack_bf16(drk_acc[c + 2 * i] * scale, drk_acc[c + 2 * i + 1] * scale);
+                  wp[i] = pack_bf16((__uint_as_float(rv[c + 2 * i]) - drk_prev[c + 2 * i]) * gsh,
+                                    (__uint_as_float(rv[c + 2 * i + 1]) - drk_prev[c + 2 * i + 1]) * gsh);
                 *reinterpret_cast<uint4*>(dst + c) = w;
               }
             }
           }
 #pragma unroll
-          for (int i = 0; i < RP / 2; ++i) drk_acc[i] = 0.f;
+          for (int i = 0; i < RP; ++i) drk_prev[i] = __uint_as_float(rv[i]);
         }
       }
     }
-    if (ok && mbar_wait(&bars[kAAllDone], 0, abort_flag, 704)) {
+    if (ok && mbar_wait(&bars[kAAllDone], 0, abort_flag, 706)) {
       tc_fence_after();
-      // each warpgroup stores its 64 of the D columns of dV and dK (D = 128) or 32 (D = 64)
+      // each warpgroup stores half of the D columns of dV and dK
       constexpr int kCols = D / 2;
-      __nv_bfloat16* dvrow = p.dv + si.b * p.dv_sb + hk * p.dv_sh + krow * p.dv_sr + hh * kCols;
-      __nv_bfloat16* dkrow = p.dk + si.b * p.dk_sb + hk * p.dk_sh + krow * p.dk_sr + hh * kCols;
+      __nv_bfloat16* dvrow = p.dv + si.b * p.dv_sb + hk * p.dv_sh + krow * p.dv_sr + wg * kCols;
+      __nv_bfloat16* dkrow = p.dk + si.b * p.dk_sb + hk * p.dk_sh + krow * p.dk_sr + wg * kCols;
 #pragma unroll 1
       for (int c = 0; c < kCols / 32; ++c) {
         uint32_t v[32];
-        tmem_ld32(tDV + lane_base + hh * kCols + 32 * c, v);
+        tmem_ld32(tDV + lane_base + wg * kCols + 32 * c, v);
         tmem_ld_wait32(v);
         if (kv_valid) store_row32(dvrow + 32 * c, v, 1.f);
-        tmem_ld32(tDK + lane_base + hh * kCols + 32 * c, v);
+        tmem_ld32(tDK + lane_base + wg * kCols + 32 * c, v);
         tmem_ld_wait32(v);
         if (kv_valid) store_row32(dkrow + 32 * c, v, scale);
+      }
+      if (wg == 0 && gh > 0 && gh == g) {
+        // dR_k of the group's last head (a graph head; otherwise it was stored at its end)
+        const int h = hk * g + gh - 1;
+        const float gsh = __ldg(P.gs + h);  // dR_k = gs * dS^T R_q
+        uint32_t rv[32];
+        if (RP == 16) {
+          tmem_ld16(tDK + lane_base + D, rv);
+          tmem_ld_wait16(rv);
+        } else {
+          tmem_ld32(tDK + lane_base + D, rv);
+          tmem_ld_wait32(rv);
+        }
+        if (kv_valid) {
+          __nv_bfloat16* dst = p.drk + si.b * p.drk_sb + h * p.drk_sh + krow * p.drk_sr;
+#pragma unroll
+          for (int c = 0; c < RP; c += 8) {
+            if (c < P.rank) {
+              uint4 w;
+              uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                wp[i] = pack_bf16((__uint_as_float(rv[c + 2 * i]) - drk_prev[c + 2 * i]) * gsh,
+                                  (__uint_as_float(rv[c + 2 * i + 1]) - drk_prev[c + 2 * i + 1]) * gsh);
+              *reinterpret_cast<uint4*>(dst + c) = w;
+            }
+          }
+        }
       }
     }
   }
@@ -909,9 +990,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
 // host-side launch (called from fna2_api.cu)
 // ---------------------------------------------------------------------------
 template <int D, int RP>
-cudaError_t launch_bwd_t(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, const CUtensorMap& dO,
-                         const CUtensorMap& rq, const CUtensorMap& rk, const BwdParams& p, cudaStream_t stream,
-                         cudaEvent_t* ev) {
+cudaError_t launch_bwd_t(const BwdMaps& m, const BwdParams& p, cudaStream_t stream, cudaEvent_t* ev) {
   const int bdim = p.prob.varlen ? 1 : p.batch;
   if (ev) {
     cudaError_t e = cudaEventRecord(ev[0], stream);
@@ -931,7 +1010,7 @@ cudaError_t launch_bwd_t(const CUtensorMap& q, const CUtensorMap& k, const CUten
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
     if (e != cudaSuccess) return e;
     dim3 grid(p.n_nblocks, p.prob.heads_kv, p.batch);
-    kern<<<grid, kDkdvThreads, L::kTotal, stream>>>(q, k, v, dO, rq, rk, p);
+    kern<<<grid, kDkdvThreads, L::kTotal, stream>>>(m.q112, m.k, m.v, m.dO112, m.rq112, m.rk, p);
     e = cudaGetLastError();
     if (e == cudaSuccess && ev) e = cudaEventRecord(ev[2], stream);
     if (e != cudaSuccess) return e;
@@ -942,7 +1021,7 @@ cudaError_t launch_bwd_t(const CUtensorMap& q, const CUtensorMap& k, const CUten
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
     if (e != cudaSuccess) return e;
     dim3 grid(p.n_mblocks, p.prob.heads, p.batch);
-    kern<<<grid, kDqThreads, L::kTotal, stream>>>(q, k, v, dO, rq, rk, p);
+    kern<<<grid, kDqThreads, L::kTotal, stream>>>(m.q, m.k, m.v, m.dO, m.rq, m.rk, p);
     e = cudaGetLastError();
     if (e == cudaSuccess && ev) e = cudaEventRecord(ev[3], stream);
     if (e != cudaSuccess) return e;
@@ -950,13 +1029,11 @@ cudaError_t launch_bwd_t(const CUtensorMap& q, const CUtensorMap& k, const CUten
   return cudaSuccess;
 }
 
-cudaError_t launch_bwd(int D, int RP, const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
-                       const CUtensorMap& dO, const CUtensorMap& rq, const CUtensorMap& rk, const BwdParams& p,
-                       cudaStream_t stream, cudaEvent_t* ev) {
-  if (D == 64 && RP == 16) return launch_bwd_t<64, 16>(q, k, v, dO, rq, rk, p, stream, ev);
-  if (D == 64 && RP == 32) return launch_bwd_t<64, 32>(q, k, v, dO, rq, rk, p, stream, ev);
-  if (D == 128 && RP == 16) return launch_bwd_t<128, 16>(q, k, v, dO, rq, rk, p, stream, ev);
-  if (D == 128 && RP == 32) return launch_bwd_t<128, 32>(q, k, v, dO, rq, rk, p, stream, ev);
+cudaError_t launch_bwd(int D, int RP, const BwdMaps& m, const BwdParams& p, cudaStream_t stream, cudaEvent_t* ev) {
+  if (D == 64 && RP == 16) return launch_bwd_t<64, 16>(m, p, stream, ev);
+  if (D == 64 && RP == 32) return launch_bwd_t<64, 32>(m, p, stream, ev);
+  if (D == 128 && RP == 16) return launch_bwd_t<128, 16>(m, p, stream, ev);
+  if (D == 128 && RP == 32) return launch_bwd_t<128, 32>(m, p, stream, ev);
   return cudaErrorInvalidValue;
 }
 

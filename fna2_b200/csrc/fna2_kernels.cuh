@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_bf16.h>
 
 namespace fna2 {
@@ -89,6 +90,14 @@ struct BwdParams {
   int total_k_rows;
   int batch;                // dense B or varlen N
   int n_mblocks, n_nblocks;
+};
+
+// Tensor maps of one backward call: 128-row boxes for the query-stationary
+// kernel, 112-row boxes (and R_q as a zero-padded 64-column swizzle atom) for
+// the key-stationary kernel.
+struct BwdMaps {
+  CUtensorMap q, k, v, dO, rq, rk;
+  CUtensorMap q112, dO112, rq112;
 };
 
 }  // namespace fna2

@@ -117,17 +117,29 @@ extern "C" int fna2_bwd_noalloc(const Fna2BwdArgs* a, void* stream) {
     return noalloc_map(m, t.ptr, s.r, rows, s.HG, s.batch_dim(), t.stride[2], t.stride[1], t.stride[0], s.RP, 128,
                        s.RP == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B, what);
   };
-  CUtensorMap tq, tk, tv, tdo, trq, trk;
-  if (int rc = map_t(&tq, a->q, s.rows_q(), s.H, "q")) return rc;
-  if (int rc = map_t(&tk, a->k, s.rows_k(), s.HKV, "k")) return rc;
-  if (int rc = map_t(&tv, a->v, s.rows_k(), s.HKV, "v")) return rc;
-  if (int rc = map_t(&tdo, a->dout, s.rows_q(), s.H, "dout")) return rc;
+  auto map_t112 = [&](CUtensorMap* m, const Fna2Tensor& t, int rows, int heads, const char* what) {
+    return noalloc_map(m, t.ptr, s.D, rows, heads, s.batch_dim(), t.stride[2], t.stride[1], t.stride[0], 64, kQT,
+                       CU_TENSOR_MAP_SWIZZLE_128B, what);
+  };
+  auto map_rr112 = [&](CUtensorMap* m, const Fna2Tensor& t, int rows, const char* what) {
+    return noalloc_map(m, t.ptr, s.r, rows, s.HG, s.batch_dim(), t.stride[2], t.stride[1], t.stride[0], 64, kQT,
+                       CU_TENSOR_MAP_SWIZZLE_128B, what);
+  };
+  BwdMaps mp;
+  if (int rc = map_t(&mp.q, a->q, s.rows_q(), s.H, "q")) return rc;
+  if (int rc = map_t(&mp.k, a->k, s.rows_k(), s.HKV, "k")) return rc;
+  if (int rc = map_t(&mp.v, a->v, s.rows_k(), s.HKV, "v")) return rc;
+  if (int rc = map_t(&mp.dO, a->dout, s.rows_q(), s.H, "dout")) return rc;
+  if (int rc = map_t112(&mp.q112, a->q, s.rows_q(), s.H, "q")) return rc;
+  if (int rc = map_t112(&mp.dO112, a->dout, s.rows_q(), s.H, "dout")) return rc;
   if (s.HG > 0) {
-    if (int rc = map_rr(&trq, a->r_q, s.rows_q(), "r_q")) return rc;
-    if (int rc = map_rr(&trk, a->r_k, s.rows_k(), "r_k")) return rc;
+    if (int rc = map_rr(&mp.rq, a->r_q, s.rows_q(), "r_q")) return rc;
+    if (int rc = map_rr(&mp.rk, a->r_k, s.rows_k(), "r_k")) return rc;
+    if (int rc = map_rr112(&mp.rq112, a->r_q, s.rows_q(), "r_q")) return rc;
   } else {
-    trq = tq;
-    trk = tk;
+    mp.rq = mp.q;
+    mp.rk = mp.k;
+    mp.rq112 = mp.q112;
   }
   BwdParams p;
   std::memset(&p, 0, sizeof(p));
@@ -165,7 +177,7 @@ extern "C" int fna2_bwd_noalloc(const Fna2BwdArgs* a, void* stream) {
   p.n_mblocks = (s.Sq + kBlockM - 1) / kBlockM;
   p.n_nblocks = (s.Sk + kBlockN - 1) / kBlockN;
   bwd_set_workspace(&p, scratch, s.batch_dim(), s.H, s.rows_q());
-  FNA2_CUDA(launch_bwd(s.D, s.RP, tq, tk, tv, tdo, trq, trk, p, static_cast<cudaStream_t>(stream),
+  FNA2_CUDA(launch_bwd(s.D, s.RP, mp, p, static_cast<cudaStream_t>(stream),
                        reinterpret_cast<cudaEvent_t*>(a->launch_events)));
   return FNA2_OK;
 }
