@@ -284,14 +284,18 @@ extern "C" int fna2_bwd(const Fna2BwdArgs* a, void* stream) {
   if (int rc = map_qkv(&m.dO, a->dout, s, s.rows_q(), s.H, "dout")) return rc;
   if (int rc = map_qkv112(&m.q112, a->q, s, s.rows_q(), s.H, "q")) return rc;
   if (int rc = map_qkv112(&m.dO112, a->dout, s, s.rows_q(), s.H, "dout")) return rc;
+  if (int rc = map_qkv112(&m.k112, a->k, s, s.rows_k(), s.HKV, "k")) return rc;
+  if (int rc = map_qkv112(&m.v112, a->v, s, s.rows_k(), s.HKV, "v")) return rc;
   if (s.HG > 0) {
     if (int rc = map_r(&m.rq, a->r_q, s, s.rows_q(), "r_q")) return rc;
     if (int rc = map_r(&m.rk, a->r_k, s, s.rows_k(), "r_k")) return rc;
     if (int rc = map_r112(&m.rq112, a->r_q, s, s.rows_q(), "r_q")) return rc;
+    if (int rc = map_r112(&m.rk112, a->r_k, s, s.rows_k(), "r_k")) return rc;
   } else {
     m.rq = m.q;  // never dereferenced: no graph heads
     m.rk = m.k;
     m.rq112 = m.q112;
+    m.rk112 = m.k112;
   }
   BwdParams p;
   std::memset(&p, 0, sizeof(p));

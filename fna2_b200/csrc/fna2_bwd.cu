@@ -675,28 +675,35 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
 // dQ / dR_q / d_gs  (Q-stationary)
 // ---------------------------------------------------------------------------
 // One CTA per (128-row query tile, head, sequence), looping over the causally
-// visible key tiles: S = Q K^T (+ R~_q R_k^T), dP = dO V^T (full 128x128 MMAs)
-// -> eight softmax-gradient warps (thread = query row = TMEM lane; warpgroup w
-// takes key columns [64w, 64w+64)) form P while the tensor core computes dP,
-// then write dS as bf16 into the first half of their own column range
-// -> dQ += dS K, dR_q += dS R_k (TS form).
-// TMEM columns: dQ [0,128) dR_q [128,128+r_pad) S [256,384) dP [384,512).
+// visible 112-row key tiles.  dR_q rides along with dQ as extra accumulator
+// columns: the B operand of the dQ MMA is [K | R_k] (R_k as a zero-padded
+// third 64-column swizzle atom next to K's two), so one N = D + r_pad MMA per
+// k-step yields dQ and dS R_k together.
+// TMEM columns: [dQ | dS R_k] [0,160) S [160,272) dP [272,384).
+// Per key tile (112 columns; warpgroup 0 owns [0,64), warpgroup 1 [64,112);
+// thread = query row = TMEM lane):
+//   S = Q K^T (+ R~_q R_k^T) -> warps: P = exp2(S*c - LSE2) in registers
+//   dP = dO V^T              -> warps: dS = P (dP - Delta) as bf16 into the
+//                               first half of their own dP columns
+//   [dQ | dS R_k] += dS [K | R_k]   (TS form)
+// The next tile's S is issued as soon as the warps have read S, so it runs
+// while they form dS; dQ and the next dP run while they form the next P.
 template <int D, int RP>
 struct DqSmem {
-  static constexpr int kTile = 128 * D * 2;
-  static constexpr int kR = 128 * RP * 2;
-  static constexpr int kChunk = 128 * 128;
+  static constexpr int kQTile = 128 * D * 2;
+  static constexpr int kQChunk = 128 * 128;
+  static constexpr int kKChunk = kQT * 128;            // one 64-column atom of a 112-row key tile
+  static constexpr int kKAtoms = D / 64 + 1;           // K chunks + the padded R_k atom
+  static constexpr int kRq = 128 * RP * 2;
   static constexpr int align(int x) { return (x + 1023) & ~1023; }
   static constexpr int oQ = 0;
-  static constexpr int oDo = align(oQ + kTile);
-  static constexpr int oRq = align(oDo + kTile);
-  static constexpr int oK0 = align(oRq + kR);
-  static constexpr int oK1 = align(oK0 + kTile);
-  static constexpr int oV0 = align(oK1 + kTile);
-  static constexpr int oV1 = align(oV0 + kTile);
-  static constexpr int oRk0 = align(oV1 + kTile);
-  static constexpr int oRk1 = align(oRk0 + kR);
-  static constexpr int oBar = align(oRk1 + kR);
+  static constexpr int oDo = align(oQ + kQTile);
+  static constexpr int oRq = align(oDo + kQTile);
+  static constexpr int oK0 = align(oRq + kRq);                   // [K c0 | (K c1) | R_k] per stage
+  static constexpr int oK1 = align(oK0 + kKAtoms * kKChunk);
+  static constexpr int oV0 = align(oK1 + kKAtoms * kKChunk);
+  static constexpr int oV1 = align(oV0 + (D / 64) * kKChunk);
+  static constexpr int oBar = align(oV1 + (D / 64) * kKChunk);
   static constexpr int kNumBars = 16;
   static constexpr int oMisc = oBar + kNumBars * 8;
   static constexpr int kTotal = oMisc + 16 + 1024;
@@ -708,9 +715,10 @@ enum DqBar {
   kBKvFull = 2,   // +stage
   kBKvEmpty = 4,  // +stage
   kBSFull = 6,
-  kBPReady = 7,
-  kBAllDone = 8,
-  kBDPFull = 9,
+  kBDPFull = 7,
+  kBSRead = 8,    // warps have read S
+  kBDsReady = 9,
+  kBAllDone = 10,
 };
 
 constexpr int kDqThreads = 320;  // 8 softmax-gradient warps, producer, MMA
@@ -737,7 +745,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   const int hk = h / (P.heads / P.heads_kv);
   const bool graph = h < P.heads_graph;
   const int kv_end = P.causal ? min(si.len_k, q0 + kBlockM) : si.len_k;
-  const int n_tiles = kv_end > 0 ? (kv_end + kBlockN - 1) / kBlockN : 0;
+  const int n_tiles = kv_end > 0 ? (kv_end + kQT - 1) / kQT : 0;
   const int warp = warp_id();
   const int lane = lane_id();
   const int tid = threadIdx.x;
@@ -761,7 +769,8 @@ __global__ void __launch_bounds__(kDqThreads, 1)
     }
     mbar_init(&bars[kBSFull], 1);
     mbar_init(&bars[kBDPFull], 1);
-    mbar_init(&bars[kBPReady], 256);
+    mbar_init(&bars[kBSRead], 256);
+    mbar_init(&bars[kBDsReady], 256);
     mbar_init(&bars[kBAllDone], 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -774,8 +783,8 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tDQ = tmem + 0, tDRQ = tmem + 128, tS = tmem + 256, tDP = tmem + 384;
-  // TMEM column (relative to S) of the packed bf16 dS for the 16 keys of k-step kk
+  const uint32_t tDQ = tmem + 0, tS = tmem + 160, tDP = tmem + 272;
+  // TMEM column (relative to dP) of the packed bf16 dS for the 16 keys of k-step kk
   auto packed_col = [](int kk) { return (kk < 4 ? 0 : 64) + (kk & 3) * 8; };
 
   if (warp == 8) {
@@ -784,86 +793,95 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       const int qrow = si.q_start + q0;
-      mbar_expect_tx(&bars[kBQFull], 2 * L::kTile + (graph ? L::kR : 0));
+      mbar_expect_tx(&bars[kBQFull], 2 * L::kQTile + (graph ? L::kRq : 0));
 #pragma unroll
       for (int c = 0; c < D / 64; ++c) {
-        tma_load_4d(smem + L::oQ + c * L::kChunk, &tmQ, &bars[kBQFull], c * 64, qrow, h, si.b);
-        tma_load_4d(smem + L::oDo + c * L::kChunk, &tmDo, &bars[kBQFull], c * 64, qrow, h, si.b);
+        tma_load_4d(smem + L::oQ + c * L::kQChunk, &tmQ, &bars[kBQFull], c * 64, qrow, h, si.b);
+        tma_load_4d(smem + L::oDo + c * L::kQChunk, &tmDo, &bars[kBQFull], c * 64, qrow, h, si.b);
       }
       if (graph) tma_load_4d(smem + L::oRq, &tmRq, &bars[kBQFull], 0, qrow, h, si.b);
       for (int j = 0; j < n_tiles; ++j) {
         const int s = j & 1;
         if (j >= 2 && !mbar_wait(&bars[kBKvEmpty + s], ((j >> 1) - 1) & 1, abort_flag, 801)) break;
-        const int krow = si.k_start + j * kBlockN;
-        mbar_expect_tx(&bars[kBKvFull + s], 2 * L::kTile + (graph ? L::kR : 0));
+        const int krow = si.k_start + j * kQT;
+        uint8_t* sk = smem + (s ? L::oK1 : L::oK0);
+        uint8_t* sv = smem + (s ? L::oV1 : L::oV0);
+        mbar_expect_tx(&bars[kBKvFull + s], 2 * (D / 64) * L::kKChunk + (graph ? L::kKChunk : 0));
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
-          tma_load_4d(smem + (s ? L::oK1 : L::oK0) + c * L::kChunk, &tmK, &bars[kBKvFull + s], c * 64, krow, hk,
-                      si.b);
-          tma_load_4d(smem + (s ? L::oV1 : L::oV0) + c * L::kChunk, &tmV, &bars[kBKvFull + s], c * 64, krow, hk,
-                      si.b);
+          tma_load_4d(sk + c * L::kKChunk, &tmK, &bars[kBKvFull + s], c * 64, krow, hk, si.b);
+          tma_load_4d(sv + c * L::kKChunk, &tmV, &bars[kBKvFull + s], c * 64, krow, hk, si.b);
         }
-        if (graph) tma_load_4d(smem + (s ? L::oRk1 : L::oRk0), &tmRk, &bars[kBKvFull + s], 0, krow, h, si.b);
+        if (graph) tma_load_4d(sk + (D / 64) * L::kKChunk, &tmRk, &bars[kBKvFull + s], 0, krow, h, si.b);
       }
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, 0, 0);
-      constexpr uint32_t idesc_dq = make_idesc_bf16(128, D, 0, 1);
-      constexpr uint32_t idesc_drq = make_idesc_bf16(128, RP, 0, 1);
+      constexpr uint32_t idesc_s = make_idesc_bf16(128, kQT, 0, 0);       // S, dP (N = 112 keys)
+      constexpr uint32_t idesc_dq = make_idesc_bf16(128, D, 0, 1);        // dQ only (vanilla heads)
+      constexpr uint32_t idesc_dqr = make_idesc_bf16(128, D + RP, 0, 1);  // [dQ | dS R_k]
       const uint32_t r_layout = r_layout_of(RP);
       const uint32_t r_sbo = 8 * RP * 2;
       const uint32_t sQ = smem_u32(smem + L::oQ), sDo = smem_u32(smem + L::oDo), sRq = smem_u32(smem + L::oRq);
-      bool ok = mbar_wait(&bars[kBQFull], 0, abort_flag, 901);
-      if (ok && graph) ok = mbar_wait(&bars[kBRqReady], 0, abort_flag, 902);
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        const int s = j & 1;
-        const uint32_t sK = smem_u32(smem + (s ? L::oK1 : L::oK0));
-        const uint32_t sV = smem_u32(smem + (s ? L::oV1 : L::oV0));
-        const uint32_t sRk = smem_u32(smem + (s ? L::oRk1 : L::oRk0));
-        if (!mbar_wait(&bars[kBKvFull + s], (j >> 1) & 1, abort_flag, 903)) break;
-        tc_fence_after();
-        // S and dP overwrite the previous tile's dS, read by the dQ MMAs issued before (in order)
+      auto stage_k = [&](int j) { return smem_u32(smem + ((j & 1) ? L::oK1 : L::oK0)); };
+      auto stage_v = [&](int j) { return smem_u32(smem + ((j & 1) ? L::oV1 : L::oV0)); };
+      auto issue_s = [&](int j) {  // S = Q K^T (+ R~_q R_k^T)
+        const uint32_t sK = stage_k(j);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * L::kChunk + (kk & 3) * 32;
-          mma_ss(tS, make_sdesc(sQ + off, 16, 1024, kSwizzle128B), make_sdesc(sK + off, 16, 1024, kSwizzle128B),
-                 idesc_s, kk > 0);
-        }
+        for (int kk = 0; kk < D / 16; ++kk)
+          mma_ss(tS, make_sdesc(sQ + (kk >> 2) * L::kQChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B),
+                 make_sdesc(sK + (kk >> 2) * L::kKChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B), idesc_s, kk > 0);
         if (graph) {
+          const uint32_t sRk = sK + (D / 64) * L::kKChunk;
 #pragma unroll
           for (int kk = 0; kk < RP / 16; ++kk)
-            mma_ss(tS, make_sdesc(sRq + kk * 32, 16, r_sbo, r_layout), make_sdesc(sRk + kk * 32, 16, r_sbo, r_layout),
+            mma_ss(tS, make_sdesc(sRq + kk * 32, 16, r_sbo, r_layout), make_sdesc(sRk + kk * 32, 16, 1024, kSwizzle128B),
                    idesc_s, 1);
         }
         mma_commit(&bars[kBSFull]);
+      };
+      auto issue_dp = [&](int j) {  // dP = dO V^T
+        const uint32_t sV = stage_v(j);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * L::kChunk + (kk & 3) * 32;
-          mma_ss(tDP, make_sdesc(sDo + off, 16, 1024, kSwizzle128B), make_sdesc(sV + off, 16, 1024, kSwizzle128B),
-                 idesc_s, kk > 0);
-        }
+        for (int kk = 0; kk < D / 16; ++kk)
+          mma_ss(tDP, make_sdesc(sDo + (kk >> 2) * L::kQChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B),
+                 make_sdesc(sV + (kk >> 2) * L::kKChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B), idesc_s, kk > 0);
         mma_commit(&bars[kBDPFull]);
-        if (!mbar_wait(&bars[kBPReady], j & 1, abort_flag, 904)) break;
+      };
+      bool ok = mbar_wait(&bars[kBQFull], 0, abort_flag, 901);
+      if (ok && graph) ok = mbar_wait(&bars[kBRqReady], 0, abort_flag, 902);
+      if (ok) ok = mbar_wait(&bars[kBKvFull], 0, abort_flag, 903);
+      if (ok) {
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_ts(tDQ, tS + packed_col(kk), make_sdesc(sK + kk * 2048, L::kChunk, 1024, kSwizzle128B), idesc_dq,
-                 (j > 0 || kk > 0) ? 1u : 0u);
-        if (graph) {
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            mma_ts(tDRQ, tS + packed_col(kk), make_sdesc(sRk + kk * 16 * RP * 2, 16, r_sbo, r_layout), idesc_drq,
-                   (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        mma_commit(&bars[kBKvEmpty + s]);
-        if (j == n_tiles - 1) mma_commit(&bars[kBAllDone]);
+        issue_s(0);
+        issue_dp(0);
       }
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        // next tile's S as soon as the warps have read S (it overlaps their dS work)
+        if (!mbar_wait(&bars[kBSRead], j & 1, abort_flag, 904)) break;
+        if (j + 1 < n_tiles) {
+          if (!mbar_wait(&bars[kBKvFull + ((j + 1) & 1)], ((j + 1) >> 1) & 1, abort_flag, 905)) break;
+          tc_fence_after();
+          issue_s(j + 1);
+        }
+        // [dQ | dS R_k] += dS [K | R_k]
+        if (!mbar_wait(&bars[kBDsReady], j & 1, abort_flag, 906)) break;
+        tc_fence_after();
+        const uint32_t sK = stage_k(j);
+#pragma unroll
+        for (int kk = 0; kk < kQT / 16; ++kk)
+          mma_ts(tDQ, tDP + packed_col(kk), make_sdesc(sK + kk * 2048, L::kKChunk, 1024, kSwizzle128B),
+                 graph ? idesc_dqr : idesc_dq, (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&bars[kBKvEmpty + (j & 1)]);
+        // next tile's dP (overwrites dS, read in order above)
+        if (j + 1 < n_tiles) issue_dp(j + 1);
+      }
+      if (ok) mma_commit(&bars[kBAllDone]);
     }
   } else {
     // ------------------------------------------------------------ softmax-gradient warps 0-7 (query rows)
-    const int wg = warp >> 2;
+    const int wg = warp >> 2;  // key columns [64*wg, min(64*wg+64, 112))
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int t = tid & 127;
     const int q_local = q0 + t;
@@ -874,6 +892,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
     const float delta = row_ok ? p.ws_delta[widx] : 0.f;
     const float sl2 = P.scale_log2;
     const int limit = row_ok ? (P.causal ? min(si.len_k, q_local + 1) : si.len_k) : 0;
+    constexpr int kW1 = kQT - 64;  // columns owned by warpgroup 1
     bool ok = true;
     if (graph && wg == 0) {
       ok = mbar_wait(&bars[kBQFull], 0, abort_flag, 1001);
@@ -890,43 +909,61 @@ __global__ void __launch_bounds__(kDqThreads, 1)
         break;
       }
       tc_fence_after();
-      // phase 1 (overlaps the dP MMA): P = exp2(S*c - LSE2) for this warp's 64 keys
+      // phase 1 (overlaps the dP MMA): P = exp2(S*c - LSE2) for this warp's keys
       float pf[64];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t sv[32];
-        tmem_ld32(tSw + 32 * c, sv);
-        tmem_ld_wait32(sv);
-        const int nvalid = limit - (j * kBlockN + 64 * wg + 32 * c);
-        if (nvalid < 32) {  // masked key columns get -inf exponents (ex2(-inf) = 0)
-#pragma unroll
-          for (int k = 0; k < 32; ++k)
-            if (k >= nvalid) sv[k] = __float_as_uint(-INFINITY);
+        if (c == 0 || wg == 0) {
+          tmem_ld32(tSw + 32 * c, sv);
+          tmem_ld_wait32(sv);
+        } else {
+          tmem_ld16(tSw + 32, sv);
+          tmem_ld_wait16(sv);
         }
+        const int ncol = (c == 1 && wg == 1) ? kW1 - 32 : 32;
+        const int nvalid = min(ncol, limit - (j * kQT + 64 * wg + 32 * c));
+        if (nvalid >= 32) {
 #pragma unroll
-        for (int k = 0; k < 32; ++k) pf[32 * c + k] = ex2(fmaf(__uint_as_float(sv[k]), sl2, -lse2));
+          for (int k = 0; k < 32; ++k) pf[32 * c + k] = ex2(fmaf(__uint_as_float(sv[k]), sl2, -lse2));
+        } else {
+#pragma unroll
+          for (int k = 0; k < 32; ++k)  // masked key columns: -inf exponent, ex2(-inf) = 0
+            if (k >= nvalid) sv[k] = __float_as_uint(-INFINITY);
+#pragma unroll
+          for (int k = 0; k < 32; ++k) pf[32 * c + k] = ex2(fmaf(__uint_as_float(sv[k]), sl2, -lse2));
+        }
       }
+      tc_fence_before();
+      mbar_arrive(&bars[kBSRead]);
       if (!mbar_wait(&bars[kBDPFull], j & 1, abort_flag, 1004)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      // phase 2: dS = P (dP - Delta), packed into columns this warp has already read
+      // phase 2 (overlaps the next S MMA): dS = P (dP - Delta) into this warp's dP columns
+      uint32_t dd[32];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t dp[32];
-        tmem_ld32(tDPw + 32 * c, dp);
-        tmem_ld_wait32(dp);
-        uint32_t dd[16];
+        if (c == 0 || wg == 0) {
+          tmem_ld32(tDPw + 32 * c, dp);
+          tmem_ld_wait32(dp);
+        } else {
+          tmem_ld16(tDPw + 32, dp);
+          tmem_ld_wait16(dp);
+#pragma unroll
+          for (int k = 16; k < 32; ++k) dp[k] = 0u;  // beyond the 112-column tile
+        }
 #pragma unroll
         for (int k = 0; k < 32; k += 2)
-          dd[k >> 1] = pack_bf16(pf[32 * c + k] * (__uint_as_float(dp[k]) - delta),
-                                 pf[32 * c + k + 1] * (__uint_as_float(dp[k + 1]) - delta));
-        tmem_st16(tSw + 16 * c, dd);
+          dd[16 * c + (k >> 1)] = pack_bf16(pf[32 * c + k] * (__uint_as_float(dp[k]) - delta),
+                                            pf[32 * c + k + 1] * (__uint_as_float(dp[k + 1]) - delta));
       }
+      tmem_st32(tDPw, dd);  // columns this warp has already read
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&bars[kBPReady]);
+      mbar_arrive(&bars[kBDsReady]);
     }
     if (ok && mbar_wait(&bars[kBAllDone], 0, abort_flag, 1003)) {
       tc_fence_after();
@@ -940,12 +977,13 @@ __global__ void __launch_bounds__(kDqThreads, 1)
         if (row_ok) store_row32(dqrow + 32 * c, v, scale);
       }
       if (graph && wg == 0) {
+        // dR_q = gs * dS R_k (the extra accumulator columns); d_gs += sum_r R_q * dS R_k
         uint32_t rv[32];
         if (RP == 16) {
-          tmem_ld16(tDRQ + lane_base, rv);
+          tmem_ld16(tDQ + lane_base + D, rv);
           tmem_ld_wait16(rv);
         } else {
-          tmem_ld32(tDRQ + lane_base, rv);
+          tmem_ld32(tDQ + lane_base + D, rv);
           tmem_ld_wait32(rv);
         }
         float part = 0.f;
@@ -1021,7 +1059,7 @@ cudaError_t launch_bwd_t(const BwdMaps& m, const BwdParams& p, cudaStream_t stre
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
     if (e != cudaSuccess) return e;
     dim3 grid(p.n_mblocks, p.prob.heads, p.batch);
-    kern<<<grid, kDqThreads, L::kTotal, stream>>>(m.q, m.k, m.v, m.dO, m.rq, m.rk, p);
+    kern<<<grid, kDqThreads, L::kTotal, stream>>>(m.q, m.k112, m.v112, m.dO, m.rq, m.rk112, p);
     e = cudaGetLastError();
     if (e == cudaSuccess && ev) e = cudaEventRecord(ev[3], stream);
     if (e != cudaSuccess) return e;

@@ -92,12 +92,13 @@ struct BwdParams {
   int n_mblocks, n_nblocks;
 };
 
-// Tensor maps of one backward call: 128-row boxes for the query-stationary
-// kernel, 112-row boxes (and R_q as a zero-padded 64-column swizzle atom) for
-// the key-stationary kernel.
+// Tensor maps of one backward call.  Each kernel tiles its stationary operand
+// by 128 rows and the streamed one by 112 rows; the streamed R operand is read
+// as a zero-padded 64-column swizzle atom next to Q (dK/dV) or K (dQ).
 struct BwdMaps {
-  CUtensorMap q, k, v, dO, rq, rk;
-  CUtensorMap q112, dO112, rq112;
+  CUtensorMap q, k, v, dO, rq, rk;        // 128-row boxes (R with r_pad-column boxes)
+  CUtensorMap q112, dO112, rq112;         // streamed by the key-stationary kernel
+  CUtensorMap k112, v112, rk112;          // streamed by the query-stationary kernel
 };
 
 }  // namespace fna2

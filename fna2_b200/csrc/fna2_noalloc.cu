@@ -132,14 +132,18 @@ extern "C" int fna2_bwd_noalloc(const Fna2BwdArgs* a, void* stream) {
   if (int rc = map_t(&mp.dO, a->dout, s.rows_q(), s.H, "dout")) return rc;
   if (int rc = map_t112(&mp.q112, a->q, s.rows_q(), s.H, "q")) return rc;
   if (int rc = map_t112(&mp.dO112, a->dout, s.rows_q(), s.H, "dout")) return rc;
+  if (int rc = map_t112(&mp.k112, a->k, s.rows_k(), s.HKV, "k")) return rc;
+  if (int rc = map_t112(&mp.v112, a->v, s.rows_k(), s.HKV, "v")) return rc;
   if (s.HG > 0) {
     if (int rc = map_rr(&mp.rq, a->r_q, s.rows_q(), "r_q")) return rc;
     if (int rc = map_rr(&mp.rk, a->r_k, s.rows_k(), "r_k")) return rc;
     if (int rc = map_rr112(&mp.rq112, a->r_q, s.rows_q(), "r_q")) return rc;
+    if (int rc = map_rr112(&mp.rk112, a->r_k, s.rows_k(), "r_k")) return rc;
   } else {
     mp.rq = mp.q;
     mp.rk = mp.k;
     mp.rq112 = mp.q112;
+    mp.rk112 = mp.k112;
   }
   BwdParams p;
   std::memset(&p, 0, sizeof(p));
