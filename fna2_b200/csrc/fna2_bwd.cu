@@ -675,11 +675,19 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
 // dQ / dR_q / d_gs  (Q-stationary)
 // ---------------------------------------------------------------------------
 // One CTA per (128-row query tile, head, sequence), looping over the causally
-// visible 112-row key tiles.  dR_q rides along with dQ as extra accumulator
-// columns: the B operand of the dQ MMA is [K | R_k] (R_k as a zero-padded
-// third 64-column swizzle atom next to K's two), so one N = D + r_pad MMA per
-// k-step yields dQ and dS R_k together.
-// TMEM columns: [dQ | dS R_k] [0,160) S [160,272) dP [272,384).
+// visible 112-row key tiles.  The stationary Q and dO tiles live in tensor
+// memory (A operands of the S and dP MMAs in the TS form), which leaves shared
+// memory for three-deep K and V rings.  They arrive by TMA in the V ring
+// (before its first use) and are moved to tensor memory by tcgen05.cp.  dR_q rides along with dQ as extra
+// accumulator columns: the B operand of the dQ MMA is [K | R_k] (R_k as a
+// zero-padded third 64-column swizzle atom next to K's two), so one
+// N = D + r_pad MMA per k-step yields dQ and dS R_k together.
+// TMEM columns: [dQ | dS R_k] [0,160) S [160,272) dP [272,384) Q [384,448)
+// dO [448,512).
+// Key tiles are visited from the diagonal down to the first one: the CTAs of
+// one head then read different tiles at any moment, so each tile comes from
+// HBM once and from L2 for the other CTAs, instead of all of them waiting on
+// the same misses in lockstep.
 // Per key tile (112 columns; warpgroup 0 owns [0,64), warpgroup 1 [64,112);
 // thread = query row = TMEM lane):
 //   S = Q K^T (+ R~_q R_k^T) -> warps: P = exp2(S*c - LSE2) in registers
@@ -688,37 +696,43 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
 //   [dQ | dS R_k] += dS [K | R_k]   (TS form)
 // The next tile's S is issued as soon as the warps have read S, so it runs
 // while they form dS; dQ and the next dP run while they form the next P.
+constexpr int kDqStages = 3;
+
 template <int D, int RP>
 struct DqSmem {
-  static constexpr int kQTile = 128 * D * 2;
-  static constexpr int kQChunk = 128 * 128;
   static constexpr int kKChunk = kQT * 128;            // one 64-column atom of a 112-row key tile
   static constexpr int kKAtoms = D / 64 + 1;           // K chunks + the padded R_k atom
   static constexpr int kRq = 128 * RP * 2;
   static constexpr int align(int x) { return (x + 1023) & ~1023; }
-  static constexpr int oQ = 0;
-  static constexpr int oDo = align(oQ + kQTile);
-  static constexpr int oRq = align(oDo + kQTile);
-  static constexpr int oK0 = align(oRq + kRq);                   // [K c0 | (K c1) | R_k] per stage
-  static constexpr int oK1 = align(oK0 + kKAtoms * kKChunk);
-  static constexpr int oV0 = align(oK1 + kKAtoms * kKChunk);
-  static constexpr int oV1 = align(oV0 + (D / 64) * kKChunk);
-  static constexpr int oBar = align(oV1 + (D / 64) * kKChunk);
-  static constexpr int kNumBars = 16;
+  static constexpr int oRq = 0;
+  static constexpr int oK = align(oRq + kRq);          // stage s: [K c0 | (K c1) | R_k]
+  static constexpr int kKStage = kKAtoms * kKChunk;
+  static constexpr int oV = oK + kDqStages * kKStage;  // stage s: [V c0 | (V c1)]
+  static constexpr int kVStage = (D / 64) * kKChunk;
+  static constexpr int kQChunk = 128 * 128;             // one 64-column atom of a 128-row tile
+  static constexpr int kQStage = (D / 64) * kQChunk;    // Q (then dO) staged in the V ring
+  static_assert(2 * kQStage <= kDqStages * kVStage, "Q and dO must fit in the V ring");
+  static constexpr int oBar = align(oV + kDqStages * kVStage);
+  static constexpr int kNumBars = 24;
   static constexpr int oMisc = oBar + kNumBars * 8;
   static constexpr int kTotal = oMisc + 16 + 1024;
+  static_assert(kKChunk % 1024 == 0, "swizzle atoms need 1024-byte alignment");
 };
 
 enum DqBar {
-  kBQFull = 0,
-  kBRqReady = 1,
-  kBKvFull = 2,   // +stage
-  kBKvEmpty = 4,  // +stage
-  kBSFull = 6,
-  kBDPFull = 7,
-  kBSRead = 8,    // warps have read S
-  kBDsReady = 9,
-  kBAllDone = 10,
+  kBRqFull = 0,   // R_q tile landed (graph heads)
+  kBRqReady = 1,  // R~_q scaled (one arrival per warp of warpgroup 0)
+  kBKFull = 2,    // +stage
+  kBKEmpty = 5,   // +stage
+  kBVFull = 8,    // +stage
+  kBVEmpty = 11,  // +stage
+  kBSFull = 14,
+  kBDPFull = 15,
+  kBSRead = 16,   // warps have read S (one arrival per warp)
+  kBDsReady = 17, // dS in tensor memory (one arrival per warp)
+  kBAllDone = 18,
+  kBQFull = 19,     // Q and dO tiles landed in the V ring
+  kBStageFree = 20, // Q and dO copied to tensor memory; the V ring may be filled
 };
 
 constexpr int kDqThreads = 320;  // 8 softmax-gradient warps, producer, MMA
@@ -761,16 +775,20 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   }
 
   if (tid == 0) {
+    mbar_init(&bars[kBRqFull], 1);
+    mbar_init(&bars[kBRqReady], 4);
     mbar_init(&bars[kBQFull], 1);
-    mbar_init(&bars[kBRqReady], 128);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&bars[kBKvFull + s], 1);
-      mbar_init(&bars[kBKvEmpty + s], 1);
+    mbar_init(&bars[kBStageFree], 1);
+    for (int s = 0; s < kDqStages; ++s) {
+      mbar_init(&bars[kBKFull + s], 1);
+      mbar_init(&bars[kBKEmpty + s], 1);
+      mbar_init(&bars[kBVFull + s], 1);
+      mbar_init(&bars[kBVEmpty + s], 1);
     }
     mbar_init(&bars[kBSFull], 1);
     mbar_init(&bars[kBDPFull], 1);
-    mbar_init(&bars[kBSRead], 256);
-    mbar_init(&bars[kBDsReady], 256);
+    mbar_init(&bars[kBSRead], 8);
+    mbar_init(&bars[kBDsReady], 8);
     mbar_init(&bars[kBAllDone], 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -783,7 +801,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tDQ = tmem + 0, tS = tmem + 160, tDP = tmem + 272;
+  const uint32_t tDQ = tmem + 0, tS = tmem + 160, tDP = tmem + 272, tQ = tmem + 384, tDO = tmem + 448;
   // TMEM column (relative to dP) of the packed bf16 dS for the 16 keys of k-step kk
   auto packed_col = [](int kk) { return (kk < 4 ? 0 : 64) + (kk & 3) * 8; };
 
@@ -793,26 +811,47 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       const int qrow = si.q_start + q0;
-      mbar_expect_tx(&bars[kBQFull], 2 * L::kQTile + (graph ? L::kRq : 0));
+      mbar_expect_tx(&bars[kBQFull], 2 * L::kQStage);
 #pragma unroll
       for (int c = 0; c < D / 64; ++c) {
-        tma_load_4d(smem + L::oQ + c * L::kQChunk, &tmQ, &bars[kBQFull], c * 64, qrow, h, si.b);
-        tma_load_4d(smem + L::oDo + c * L::kQChunk, &tmDo, &bars[kBQFull], c * 64, qrow, h, si.b);
+        tma_load_4d(smem + L::oV + c * L::kQChunk, &tmQ, &bars[kBQFull], c * 64, qrow, h, si.b);
+        tma_load_4d(smem + L::oV + L::kQStage + c * L::kQChunk, &tmDo, &bars[kBQFull], c * 64, qrow, h, si.b);
       }
-      if (graph) tma_load_4d(smem + L::oRq, &tmRq, &bars[kBQFull], 0, qrow, h, si.b);
-      for (int j = 0; j < n_tiles; ++j) {
-        const int s = j & 1;
-        if (j >= 2 && !mbar_wait(&bars[kBKvEmpty + s], ((j >> 1) - 1) & 1, abort_flag, 801)) break;
-        const int krow = si.k_start + j * kQT;
-        uint8_t* sk = smem + (s ? L::oK1 : L::oK0);
-        uint8_t* sv = smem + (s ? L::oV1 : L::oV0);
-        mbar_expect_tx(&bars[kBKvFull + s], 2 * (D / 64) * L::kKChunk + (graph ? L::kKChunk : 0));
+      if (graph) {
+        mbar_expect_tx(&bars[kBRqFull], L::kRq);
+        tma_load_4d(smem + L::oRq, &tmRq, &bars[kBRqFull], 0, qrow, h, si.b);
+      }
+      auto load_k = [&](int j) {
+        const int s = j % kDqStages;
+        const int krow = si.k_start + (n_tiles - 1 - j) * kQT;
+        uint8_t* sk = smem + L::oK + s * L::kKStage;
+        mbar_expect_tx(&bars[kBKFull + s], (D / 64) * L::kKChunk + (graph ? L::kKChunk : 0));
 #pragma unroll
-        for (int c = 0; c < D / 64; ++c) {
-          tma_load_4d(sk + c * L::kKChunk, &tmK, &bars[kBKvFull + s], c * 64, krow, hk, si.b);
-          tma_load_4d(sv + c * L::kKChunk, &tmV, &bars[kBKvFull + s], c * 64, krow, hk, si.b);
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_4d(sk + c * L::kKChunk, &tmK, &bars[kBKFull + s], c * 64, krow, hk, si.b);
+        if (graph) tma_load_4d(sk + (D / 64) * L::kKChunk, &tmRk, &bars[kBKFull + s], 0, krow, h, si.b);
+      };
+      auto load_v = [&](int j) {
+        const int s = j % kDqStages;
+        const int krow = si.k_start + (n_tiles - 1 - j) * kQT;
+        uint8_t* sv = smem + L::oV + s * L::kVStage;
+        mbar_expect_tx(&bars[kBVFull + s], (D / 64) * L::kKChunk);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_4d(sv + c * L::kKChunk, &tmV, &bars[kBVFull + s], c * 64, krow, hk, si.b);
+      };
+      const int n_first = min(n_tiles, kDqStages);
+      for (int j = 0; j < n_first; ++j) load_k(j);
+      // the V ring holds the Q and dO tiles until they are in tensor memory
+      if (mbar_wait(&bars[kBStageFree], 0, abort_flag, 803)) {
+        for (int j = 0; j < n_first; ++j) load_v(j);
+        for (int j = kDqStages; j < n_tiles; ++j) {
+          const uint32_t par = ((j / kDqStages) - 1) & 1;
+          if (!mbar_wait(&bars[kBKEmpty + j % kDqStages], par, abort_flag, 801)) break;
+          load_k(j);
+          if (!mbar_wait(&bars[kBVEmpty + j % kDqStages], par, abort_flag, 802)) break;
+          load_v(j);
         }
-        if (graph) tma_load_4d(sk + (D / 64) * L::kKChunk, &tmRk, &bars[kBKvFull + s], 0, krow, h, si.b);
       }
     }
   } else if (warp == 9) {
@@ -823,15 +862,15 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       constexpr uint32_t idesc_dqr = make_idesc_bf16(128, D + RP, 0, 1);  // [dQ | dS R_k]
       const uint32_t r_layout = r_layout_of(RP);
       const uint32_t r_sbo = 8 * RP * 2;
-      const uint32_t sQ = smem_u32(smem + L::oQ), sDo = smem_u32(smem + L::oDo), sRq = smem_u32(smem + L::oRq);
-      auto stage_k = [&](int j) { return smem_u32(smem + ((j & 1) ? L::oK1 : L::oK0)); };
-      auto stage_v = [&](int j) { return smem_u32(smem + ((j & 1) ? L::oV1 : L::oV0)); };
+      const uint32_t sRq = smem_u32(smem + L::oRq);
+      auto stage_k = [&](int j) { return smem_u32(smem + L::oK + (j % kDqStages) * L::kKStage); };
+      auto stage_v = [&](int j) { return smem_u32(smem + L::oV + (j % kDqStages) * L::kVStage); };
       auto issue_s = [&](int j) {  // S = Q K^T (+ R~_q R_k^T)
         const uint32_t sK = stage_k(j);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
-          mma_ss(tS, make_sdesc(sQ + (kk >> 2) * L::kQChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B),
-                 make_sdesc(sK + (kk >> 2) * L::kKChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B), idesc_s, kk > 0);
+          mma_ts(tS, tQ + kk * 8, make_sdesc(sK + (kk >> 2) * L::kKChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B),
+                 idesc_s, kk > 0);
         if (graph) {
           const uint32_t sRk = sK + (D / 64) * L::kKChunk;
 #pragma unroll
@@ -845,35 +884,58 @@ __global__ void __launch_bounds__(kDqThreads, 1)
         const uint32_t sV = stage_v(j);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
-          mma_ss(tDP, make_sdesc(sDo + (kk >> 2) * L::kQChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B),
-                 make_sdesc(sV + (kk >> 2) * L::kKChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B), idesc_s, kk > 0);
+          mma_ts(tDP, tDO + kk * 8, make_sdesc(sV + (kk >> 2) * L::kKChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B),
+                 idesc_s, kk > 0);
         mma_commit(&bars[kBDPFull]);
+        mma_commit(&bars[kBVEmpty + (j % kDqStages)]);
       };
+      // Q and dO: shared memory (V ring) -> tensor memory, in the TS A-operand layout
       bool ok = mbar_wait(&bars[kBQFull], 0, abort_flag, 901);
+      if (ok) {
+        tc_fence_after();
+        const uint32_t sQ = smem_u32(smem + L::oV), sDo = sQ + L::kQStage;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * L::kQChunk + (kk & 3) * 32;
+          tmem_cp_128x256b(tQ + kk * 8, make_sdesc(sQ + off, 16, 1024, kSwizzle128B));
+          tmem_cp_128x256b(tDO + kk * 8, make_sdesc(sDo + off, 16, 1024, kSwizzle128B));
+        }
+        mma_commit(&bars[kBStageFree]);
+      }
       if (ok && graph) ok = mbar_wait(&bars[kBRqReady], 0, abort_flag, 902);
-      if (ok) ok = mbar_wait(&bars[kBKvFull], 0, abort_flag, 903);
+      if (ok) ok = mbar_wait_spin(&bars[kBKFull], 0, abort_flag, 903);
       if (ok) {
         tc_fence_after();
         issue_s(0);
-        issue_dp(0);
+        ok = mbar_wait_spin(&bars[kBVFull], 0, abort_flag, 907);
+        if (ok) {
+          tc_fence_after();
+          issue_dp(0);
+        }
       }
       for (int j = 0; ok && j < n_tiles; ++j) {
         // next tile's S as soon as the warps have read S (it overlaps their dS work)
-        if (!mbar_wait(&bars[kBSRead], j & 1, abort_flag, 904)) break;
+        if (!mbar_wait_spin(&bars[kBSRead], j & 1, abort_flag, 904)) break;
         if (j + 1 < n_tiles) {
-          if (!mbar_wait(&bars[kBKvFull + ((j + 1) & 1)], ((j + 1) >> 1) & 1, abort_flag, 905)) break;
+          const int s1 = (j + 1) % kDqStages;
+          if (!mbar_wait_spin(&bars[kBKFull + s1], ((j + 1) / kDqStages) & 1, abort_flag, 905)) break;
           tc_fence_after();
           issue_s(j + 1);
         }
-        // [dQ | dS R_k] += dS [K | R_k]
-        if (!mbar_wait(&bars[kBDsReady], j & 1, abort_flag, 906)) break;
+        // [dQ | dS R_k] += dS [K | R_k], then the next dP.  Both waits come
+        // before the two MMA groups: a wait issued behind queued MMAs only
+        // returns once the tensor pipe has nearly drained them.
+        if (!mbar_wait_spin(&bars[kBDsReady], j & 1, abort_flag, 906)) break;
+        if (j + 1 < n_tiles &&
+            !mbar_wait_spin(&bars[kBVFull + (j + 1) % kDqStages], ((j + 1) / kDqStages) & 1, abort_flag, 908))
+          break;
         tc_fence_after();
         const uint32_t sK = stage_k(j);
 #pragma unroll
         for (int kk = 0; kk < kQT / 16; ++kk)
           mma_ts(tDQ, tDP + packed_col(kk), make_sdesc(sK + kk * 2048, L::kKChunk, 1024, kSwizzle128B),
                  graph ? idesc_dqr : idesc_dq, (j > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(&bars[kBKvEmpty + (j & 1)]);
+        mma_commit(&bars[kBKEmpty + (j % kDqStages)]);
         // next tile's dP (overwrites dS, read in order above)
         if (j + 1 < n_tiles) issue_dp(j + 1);
       }
@@ -892,15 +954,25 @@ __global__ void __launch_bounds__(kDqThreads, 1)
     const float delta = row_ok ? p.ws_delta[widx] : 0.f;
     const float sl2 = P.scale_log2;
     const int limit = row_ok ? (P.causal ? min(si.len_k, q_local + 1) : si.len_k) : 0;
-    constexpr int kW1 = kQT - 64;  // columns owned by warpgroup 1
     bool ok = true;
+    // raw R_q row for d_gs, fetched now and used in the epilogue
+    uint4 rq_raw[RP / 8];
+#pragma unroll
+    for (int c = 0; c < RP / 8; ++c) rq_raw[c] = make_uint4(0u, 0u, 0u, 0u);
+    if (graph && wg == 0 && row_ok) {
+      const uint4* src = reinterpret_cast<const uint4*>(p.rq + si.b * p.rq_sb + h * p.rq_sh + row * p.rq_sr);
+#pragma unroll
+      for (int c = 0; c < RP / 8; ++c)
+        if (8 * c < P.rank) rq_raw[c] = __ldg(src + c);
+    }
     if (graph && wg == 0) {
-      ok = mbar_wait(&bars[kBQFull], 0, abort_flag, 1001);
+      ok = mbar_wait(&bars[kBRqFull], 0, abort_flag, 1001);
       if (ok) {
         scale_rows_inplace<RP>(smem + L::oRq, t, __ldg(P.gs + h) / scale);
         fence_proxy_async_smem();
       }
-      mbar_arrive(&bars[kBRqReady]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[kBRqReady]);
     }
     const uint32_t tSw = tS + lane_base + 64 * wg, tDPw = tDP + lane_base + 64 * wg;
     for (int j = 0; ok && j < n_tiles; ++j) {
@@ -914,28 +986,34 @@ __global__ void __launch_bounds__(kDqThreads, 1)
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t sv[32];
+        const int col0 = (n_tiles - 1 - j) * kQT + 64 * wg + 32 * c;
         if (c == 0 || wg == 0) {
           tmem_ld32(tSw + 32 * c, sv);
           tmem_ld_wait32(sv);
-        } else {
+          if (col0 + 32 > limit) {
+#pragma unroll
+            for (int k = 0; k < 32; ++k)  // masked key columns: -inf exponent, ex2(-inf) = 0
+              if (col0 + k >= limit) sv[k] = __float_as_uint(-INFINITY);
+          }
+#pragma unroll
+          for (int k = 0; k < 32; ++k) pf[32 * c + k] = ex2(fmaf(__uint_as_float(sv[k]), sl2, -lse2));
+        } else {  // warpgroup 1, keys 96..111 of the tile
           tmem_ld16(tSw + 32, sv);
           tmem_ld_wait16(sv);
-        }
-        const int ncol = (c == 1 && wg == 1) ? kW1 - 32 : 32;
-        const int nvalid = min(ncol, limit - (j * kQT + 64 * wg + 32 * c));
-        if (nvalid >= 32) {
+          if (col0 + 16 > limit) {
 #pragma unroll
-          for (int k = 0; k < 32; ++k) pf[32 * c + k] = ex2(fmaf(__uint_as_float(sv[k]), sl2, -lse2));
-        } else {
+            for (int k = 0; k < 16; ++k)
+              if (col0 + k >= limit) sv[k] = __float_as_uint(-INFINITY);
+          }
 #pragma unroll
-          for (int k = 0; k < 32; ++k)  // masked key columns: -inf exponent, ex2(-inf) = 0
-            if (k >= nvalid) sv[k] = __float_as_uint(-INFINITY);
+          for (int k = 0; k < 16; ++k) pf[32 + k] = ex2(fmaf(__uint_as_float(sv[k]), sl2, -lse2));
 #pragma unroll
-          for (int k = 0; k < 32; ++k) pf[32 * c + k] = ex2(fmaf(__uint_as_float(sv[k]), sl2, -lse2));
+          for (int k = 16; k < 32; ++k) pf[32 + k] = 0.f;
         }
       }
       tc_fence_before();
-      mbar_arrive(&bars[kBSRead]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[kBSRead]);
       if (!mbar_wait(&bars[kBDPFull], j & 1, abort_flag, 1004)) {
         ok = false;
         break;
@@ -963,7 +1041,8 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       tmem_st32(tDPw, dd);  // columns this warp has already read
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&bars[kBDsReady]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[kBDsReady]);
     }
     if (ok && mbar_wait(&bars[kBAllDone], 0, abort_flag, 1003)) {
       tc_fence_after();
@@ -989,13 +1068,11 @@ __global__ void __launch_bounds__(kDqThreads, 1)
         float part = 0.f;
         if (row_ok) {
           const float gsh = __ldg(P.gs + h);
-          const __nv_bfloat16* rq = p.rq + si.b * p.rq_sb + h * p.rq_sh + row * p.rq_sr;
           __nv_bfloat16* dst = p.drq + si.b * p.drq_sb + h * p.drq_sh + row * p.drq_sr;
 #pragma unroll
           for (int c = 0; c < RP; c += 8) {
             if (c >= P.rank) break;
-            const uint4 rw = *reinterpret_cast<const uint4*>(rq + c);
-            const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rw);
+            const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rq_raw[c / 8]);
             uint4 w;
             uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
 #pragma unroll

@@ -66,6 +66,8 @@ struct BwdParams {
   int64_t o_sb, o_sh, o_sr;
   const __nv_bfloat16* dout;
   int64_t do_sb, do_sh, do_sr;
+  const __nv_bfloat16* q;  // read row-wise into tensor memory by the query-stationary kernel
+  int64_t q_sb, q_sh, q_sr;
   const float* lse;  // forward LSE, index (b*H + h) * lse_sbh + row
   int64_t lse_sbh;
   // workspace: per (b*H + h) rows of log2-domain LSE and Delta = rowsum(dO*O)

@@ -158,6 +158,8 @@ extern "C" int fna2_bwd_noalloc(const Fna2BwdArgs* a, void* stream) {
   set3(a->out, &p.o_sb, &p.o_sh, &p.o_sr);
   p.dout = static_cast<const __nv_bfloat16*>(a->dout.ptr);
   set3(a->dout, &p.do_sb, &p.do_sh, &p.do_sr);
+  p.q = static_cast<const __nv_bfloat16*>(a->q.ptr);
+  set3(a->q, &p.q_sb, &p.q_sh, &p.q_sr);
   p.lse = a->lse;
   p.lse_sbh = s.rows_q();
   p.dq = static_cast<__nv_bfloat16*>(a->dq.ptr);

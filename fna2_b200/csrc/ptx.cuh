@@ -91,6 +91,43 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   return mbar_wait_slow(bar, parity, abort_flag, site);
 }
 
+// Non-suspending variant for the MMA-issuing thread: polls with test_wait so
+// that a completed phase is seen within a few cycles (a suspended try_wait can
+// sleep for hundreds of cycles past the phase completion while the tensor
+// pipe drains). Same bound and abort semantics as mbar_wait.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __noinline__ static bool mbar_spin_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                   int site) {
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 256; ++i)
+      if (mbar_test_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      *abort_flag = 1;
+      atomicCAS(&g_device_error, 0, site);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int site) {
+  if (mbar_test_wait(bar, parity)) return true;
+  return mbar_spin_slow(bar, parity, abort_flag, site);
+}
+
 // ---------------------------------------------------------------------------
 // TMA (bulk tensor copies, global -> shared, no multicast)
 // ---------------------------------------------------------------------------
@@ -189,6 +226,14 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
 }
 // Arrive (once) on `bar` when all previously issued tcgen05 async ops of this
 // thread have completed.
+// Shared memory -> tensor memory copy of a 128-row x 32-byte slice described
+// by a shared-memory matrix descriptor (same layout rules as an MMA operand):
+// row i lands in lane i, 8 consecutive 32-bit columns. Asynchronous; ordered
+// before later tcgen05.mma of the same thread and tracked by tcgen05.commit.
+__device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
