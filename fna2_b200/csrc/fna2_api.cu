@@ -167,14 +167,17 @@ int map_qkv(CUtensorMap* m, const Fna2Tensor& t, const Shape& s, int rows, int h
   return make_map(m, t.ptr, s.D, rows, heads, s.batch_dim(), t.stride[2], t.stride[1], t.stride[0], 64, 128,
                   CU_TENSOR_MAP_SWIZZLE_128B, what);
 }
-// The key-stationary backward kernel tiles queries by 112 rows and reads R_q
-// as a third 64-column SW128 atom next to Q (columns past r zero-filled).
-int map_qkv112(CUtensorMap* m, const Fna2Tensor& t, const Shape& s, int rows, int heads, const char* what) {
-  return make_map(m, t.ptr, s.D, rows, heads, s.batch_dim(), t.stride[2], t.stride[1], t.stride[0], 64, kQT,
+// The backward kernels stream their non-stationary operand in tiles of
+// box_rows rows (query tiles of dkdv_query_rows rows in the key-stationary
+// kernel, 112-row key tiles in the query-stationary one) and read the streamed
+// R as a 64-column SW128 atom beside it (columns past r zero-filled).
+int map_qkv_tile(CUtensorMap* m, const Fna2Tensor& t, const Shape& s, int rows, int heads, int box_rows,
+                 const char* what) {
+  return make_map(m, t.ptr, s.D, rows, heads, s.batch_dim(), t.stride[2], t.stride[1], t.stride[0], 64, box_rows,
                   CU_TENSOR_MAP_SWIZZLE_128B, what);
 }
-int map_r112(CUtensorMap* m, const Fna2Tensor& t, const Shape& s, int rows, const char* what) {
-  return make_map(m, t.ptr, s.r, rows, s.HG, s.batch_dim(), t.stride[2], t.stride[1], t.stride[0], 64, kQT,
+int map_r_tile(CUtensorMap* m, const Fna2Tensor& t, const Shape& s, int rows, int box_rows, const char* what) {
+  return make_map(m, t.ptr, s.r, rows, s.HG, s.batch_dim(), t.stride[2], t.stride[1], t.stride[0], 64, box_rows,
                   CU_TENSOR_MAP_SWIZZLE_128B, what);
 }
 int map_r(CUtensorMap* m, const Fna2Tensor& t, const Shape& s, int rows, const char* what) {
@@ -282,19 +285,20 @@ extern "C" int fna2_bwd(const Fna2BwdArgs* a, void* stream) {
   if (int rc = map_qkv(&m.k, a->k, s, s.rows_k(), s.HKV, "k")) return rc;
   if (int rc = map_qkv(&m.v, a->v, s, s.rows_k(), s.HKV, "v")) return rc;
   if (int rc = map_qkv(&m.dO, a->dout, s, s.rows_q(), s.H, "dout")) return rc;
-  if (int rc = map_qkv112(&m.q112, a->q, s, s.rows_q(), s.H, "q")) return rc;
-  if (int rc = map_qkv112(&m.dO112, a->dout, s, s.rows_q(), s.H, "dout")) return rc;
-  if (int rc = map_qkv112(&m.k112, a->k, s, s.rows_k(), s.HKV, "k")) return rc;
-  if (int rc = map_qkv112(&m.v112, a->v, s, s.rows_k(), s.HKV, "v")) return rc;
+  const int qs_rows = dkdv_query_rows(s.D, s.RP);
+  if (int rc = map_qkv_tile(&m.qS, a->q, s, s.rows_q(), s.H, qs_rows, "q")) return rc;
+  if (int rc = map_qkv_tile(&m.dOS, a->dout, s, s.rows_q(), s.H, qs_rows, "dout")) return rc;
+  if (int rc = map_qkv_tile(&m.k112, a->k, s, s.rows_k(), s.HKV, kQT, "k")) return rc;
+  if (int rc = map_qkv_tile(&m.v112, a->v, s, s.rows_k(), s.HKV, kQT, "v")) return rc;
   if (s.HG > 0) {
     if (int rc = map_r(&m.rq, a->r_q, s, s.rows_q(), "r_q")) return rc;
     if (int rc = map_r(&m.rk, a->r_k, s, s.rows_k(), "r_k")) return rc;
-    if (int rc = map_r112(&m.rq112, a->r_q, s, s.rows_q(), "r_q")) return rc;
-    if (int rc = map_r112(&m.rk112, a->r_k, s, s.rows_k(), "r_k")) return rc;
+    if (int rc = map_r_tile(&m.rqS, a->r_q, s, s.rows_q(), qs_rows, "r_q")) return rc;
+    if (int rc = map_r_tile(&m.rk112, a->r_k, s, s.rows_k(), kQT, "r_k")) return rc;
   } else {
     m.rq = m.q;  // never dereferenced: no graph heads
     m.rk = m.k;
-    m.rq112 = m.q112;
+    m.rqS = m.qS;
     m.rk112 = m.k112;
   }
   BwdParams p;

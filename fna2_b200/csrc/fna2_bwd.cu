@@ -14,19 +14,20 @@
 //                         to no sequence, as the reference's zeros_like does.
 //   fna2_bwd_dkdv_kernel  one CTA per (128-row key tile, KV head, sequence),
 //                         looping over the query heads of the GQA group and
-//                         the causally visible query tiles.  TMEM: dV, dK
-//                         accumulators; S^T = K Q^T + R_k R~_q^T and
-//                         dP^T = V dO^T per step; the softmax warps write P^T
-//                         and dS^T back into TMEM as bf16 and the TS-form MMAs
-//                         dV += P^T dO, dK += dS^T Q, dR_k-tile = dS^T R~_q
+//                         the causally visible query tiles.  TMEM: dV and
+//                         [dK | dR_k] accumulators; S^T = K Q^T + R~_k R_q^T
+//                         and dP^T = V dO^T per step; the softmax warps write
+//                         P^T and dS^T back into TMEM as bf16 and the TS-form
+//                         MMAs dV += P^T dO, [dK | dR_k] += dS^T [Q | R_q]
 //                         read them from there.  No dK/dV atomics.
 //   fna2_bwd_dq_kernel    one CTA per (128-row query tile, head, sequence),
 //                         looping over the causally visible key tiles:
 //                         S, dP, dS (bf16 into TMEM), dQ += dS K and
 //                         dR_q += dS R_k (TS-form), then d_gs via one atomic
 //                         per warp.
-// R~_q = R_q * gs/scale is staged in shared memory so the bias is one extra
-// K-slice (K = r_pad) of the score MMA; dR_k = scale * dS^T R~_q follows.
+// The rank-r bias is one extra K-slice (K = r_pad) of each score MMA, with one
+// side pre-scaled by gs/scale in shared memory (R~_k in the dK/dV kernel, R~_q
+// in the dQ kernel).
 #include "fna2_kernels.cuh"
 #include "ptx.cuh"
 
@@ -140,95 +141,159 @@ __device__ __forceinline__ uint32_t r_layout_of(int rp) {
 // dK / dV / dR_k  (KV-stationary)
 // ---------------------------------------------------------------------------
 // One CTA per (128-row key tile, KV head, sequence), looping over the query
-// heads of the GQA group and the causally visible 112-row query tiles.
+// heads of the GQA group and the causally visible query tiles of QT rows
+// (dkdv_query_rows: 96, or 64 for head_dim 128 with r_pad 32).
 //
 // The bias enters the score MMA as R~_k R_q^T with R~_k = R_k*gs/scale, scaled
 // in shared memory once per head.  dR_k rides along with dK as extra
 // accumulator columns: the B operand of the dK MMA is [Q | R_q] (R_q stored as
-// a zero-padded third 64-column swizzle atom next to Q's two), so one
-// N = D + r_pad MMA per k-step yields dK and dS^T R_q (dR_k = gs * that).  112-row query tiles are what make the extra
-// columns fit in TMEM:
-//   dV [0,128) | dK,dR_k [128,288) | S^T [288,400) | dP^T [400,512)
-// Per query tile (112 columns; warpgroup 0 owns columns [0,64), warpgroup 1
-// [64,112), each thread one key row = TMEM lane):
+// a zero-padded 64-column swizzle atom after Q's), so one N = D + r_pad MMA
+// per k-step yields dK and dS^T R_q (dR_k = gs * that).
+//
+// TMEM columns: dV [0,D) | dK,dR_k [D,2D+r_pad) | S^T (QT) | dP^T (QT) | P^T
+// (QT/2, packed bf16).  P^T has its own columns so that the next tile's S^T
+// can be computed as soon as the warps have read S^T; dS^T is packed into
+// the first half of each warpgroup's own dP^T columns.
+// Per query tile (warpgroup w owns query columns [w*QT/2, (w+1)*QT/2), each
+// thread one key row = TMEM lane):
 //   tensor core:  S^T = K Q^T (+ R~_k R_q^T), dP^T = V dO^T  (SS)
-//   warps:        P^T = exp2(S^T*c - LSE2) -> bf16 into the first half of each
-//                 warpgroup's own S^T columns; dS^T = P^T (dP^T - Delta)
-//                 likewise into dP^T
+//   warps:        P^T = exp2(S^T*c - LSE2) (bf16), dS^T = P^T (dP^T - Delta)
 //   tensor core:  dV += P^T dO, [dK | dR_k] += dS^T [Q | R_q]  (TS form)
-// The MMA stream runs the next tile's S^T (its stage was loaded a tile ahead)
-// while the warps form dS^T, and dK plus the next dP^T while they form the next
-// P^T.
-constexpr int kQT = 112;  // query rows per backward (dK/dV) tile
+// Two threads issue MMAs: one the S^T and dP^T groups, the other the dV and
+// dK groups, so that neither waits on a barrier behind its own queued MMAs
+// while the other's are executing.  The only cross-stream hazard, dP^T of
+// the next tile overwriting the dS^T that dK reads, is ordered by a barrier.
+template <int D, int RP>
+struct DkdvCfg {
+  static constexpr int QT = dkdv_query_rows(D, RP);
+  static constexpr int QH = QT / 2;  // query columns per warpgroup
+  static constexpr int tDV = 0, tDK = D, tS = 2 * D + RP, tDP = tS + QT, tPT = tDP + QT;
+  static_assert(tPT + QT / 2 <= 512, "TMEM budget");
+  static_assert(QH == 32 || QH == 48, "warpgroup column split");
+};
 
 template <int D, int RP>
 struct DkdvSmem {
+  static constexpr int QT = DkdvCfg<D, RP>::QT;
   static constexpr int kKTile = 128 * D * 2;
   static constexpr int kKChunk = 128 * 128;
-  static constexpr int kQChunk = kQT * 128;            // one 64-column swizzle atom of a 112-row tile
-  static constexpr int kQAtoms = D / 64 + 1;           // Q chunks + the padded R~_q atom
+  static constexpr int kQChunk = QT * 128;             // one 64-column swizzle atom of a query tile
+  static constexpr int kQAtoms = D / 64 + 1;           // Q chunks + the padded R_q atom
   static constexpr int kRk = 128 * RP * 2;
   static constexpr int align(int x) { return (x + 1023) & ~1023; }
   static constexpr int oK = 0;
   static constexpr int oV = align(oK + kKTile);
   static constexpr int oRk = align(oV + kKTile);
-  static constexpr int oQ0 = align(oRk + kRk);                 // [Q c0 | (Q c1) | R~_q] per stage
+  static constexpr int oQ0 = align(oRk + kRk);                 // [Q c0 | (Q c1) | R_q] per stage
   static constexpr int oQ1 = align(oQ0 + kQAtoms * kQChunk);
   static constexpr int oDo0 = align(oQ1 + kQAtoms * kQChunk);
   static constexpr int oDo1 = align(oDo0 + (D / 64) * kQChunk);
   static constexpr int oVec = align(oDo1 + (D / 64) * kQChunk);  // [2 stages][lse2 128 | delta 128] floats
   static constexpr int oBar = oVec + 2 * 256 * 4;
-  static constexpr int kNumBars = 20;
+  static constexpr int kNumBars = 24;
   static constexpr int oMisc = oBar + kNumBars * 8;
   static constexpr int kTotal = oMisc + 16 + 1024;
+  static_assert(kQChunk % 1024 == 0, "swizzle atoms need 1024-byte alignment");
 };
 
 enum DkdvBar {
   kAKV = 0,
   kARkFull = 1,
   kARkEmpty = 2,
-  kAQFull = 3,    // +stage
-  kAQEmpty = 5,   // +stage
-  kAPrep = 7,     // +stage
-  kASFull = 9,
-  kADPFull = 10,
-  kAPReady = 11,
-  kADsReady = 12,
-  kAHeadDone = 13,
-  kAAllDone = 14,
-  kARkReady = 15,  // R~_k scaled in shared memory (once per graph head)
+  kAQFull = 3,     // +stage: Q and R_q of a query tile
+  kAQEmpty = 5,    // +stage (last reader: dK)
+  kADoFull = 7,    // +stage: dO of a query tile (loaded behind Q)
+  kADoEmpty = 9,   // +stage (last reader: dV)
+  kAPrep = 11,     // +stage: lse2/Delta rows in shared memory
+  kASFull = 13,
+  kADPFull = 14,
+  kASRead = 15,    // warps have read S^T (one arrival per warp)
+  kAPReady = 16,   // P^T in TMEM (one arrival per warp)
+  kADsReady = 17,  // dS^T in TMEM (one arrival per warp)
+  kADvDone = 18,   // dV MMA of a tile complete (P^T columns free)
+  kADkDone = 19,   // dK MMA of a tile complete (dS^T columns free)
+  kAHeadDone = 20,
+  kAAllDone = 21,
+  kARkReady = 22,  // R~_k scaled in shared memory (once per graph head)
 };
 
-constexpr int kDkdvThreads = 352;  // 8 softmax-gradient warps, producer, MMA, prep
+constexpr int kDkdvThreads = 384;  // 8 softmax-gradient warps, producer, MMA (S/dP), prep, MMA (dV/dK)
 
-// P^T for one chunk of up to 32 query columns [qb, qb+ncol) of one key row:
+// P^T for one chunk of 32 query columns [qb, qb+32) of one key row:
 // exp2(S^T*c - LSE2), packed into pk[o .. o+16).  Columns outside [q_lo, q_hi)
-// (causal, sequence end) and past ncol get exactly 0.
-__device__ __forceinline__ void p_chunk_bwd(uint32_t (&sv)[32], uint32_t (&pk)[32], const int o, const int qb,
-                                            const int ncol, const int q_lo, const int q_hi, const float* lv,
-                                            const float sl2) {
-  if (ncol == 32 && qb >= q_lo && qb + 32 <= q_hi) {
+// (causal, sequence end) get exactly 0.
+template <int N>
+__device__ __forceinline__ void p_chunk_bwd(const uint32_t* sv_in, uint32_t* pk, const int qb, const int q_lo,
+                                            const int q_hi, const float* lv, const float sl2) {
+  uint32_t sv[N];
 #pragma unroll
-    for (int k = 0; k < 32; k += 4) {
-      const float4 l4 = *reinterpret_cast<const float4*>(&lv[qb + k]);
-      pk[o + (k >> 1)] = pack_bf16(ex2(fmaf(__uint_as_float(sv[k]), sl2, -l4.x)),
-                                   ex2(fmaf(__uint_as_float(sv[k + 1]), sl2, -l4.y)));
-      pk[o + (k >> 1) + 1] = pack_bf16(ex2(fmaf(__uint_as_float(sv[k + 2]), sl2, -l4.z)),
-                                       ex2(fmaf(__uint_as_float(sv[k + 3]), sl2, -l4.w)));
-    }
-  } else {
+  for (int k = 0; k < N; ++k) sv[k] = sv_in[k];
+  if (!(qb >= q_lo && qb + N <= q_hi)) {
 #pragma unroll
-    for (int k = 0; k < 32; ++k) {  // masked columns: -inf exponent, ex2(-inf) = 0
+    for (int k = 0; k < N; ++k) {  // masked columns: -inf exponent, ex2(-inf) = 0
       const int qi = qb + k;
-      if (!(k < ncol && qi >= q_lo && qi < q_hi)) sv[k] = __float_as_uint(-INFINITY);
+      if (!(qi >= q_lo && qi < q_hi)) sv[k] = __float_as_uint(-INFINITY);
     }
+  }
 #pragma unroll
-    for (int k = 0; k < 32; k += 4) {
-      const float4 l4 = *reinterpret_cast<const float4*>(&lv[qb + k]);
-      pk[o + (k >> 1)] = pack_bf16(ex2(fmaf(__uint_as_float(sv[k]), sl2, -l4.x)),
-                                   ex2(fmaf(__uint_as_float(sv[k + 1]), sl2, -l4.y)));
-      pk[o + (k >> 1) + 1] = pack_bf16(ex2(fmaf(__uint_as_float(sv[k + 2]), sl2, -l4.z)),
-                                       ex2(fmaf(__uint_as_float(sv[k + 3]), sl2, -l4.w)));
+  for (int k = 0; k < N; k += 4) {
+    const float4 l4 = *reinterpret_cast<const float4*>(&lv[qb + k]);
+    pk[k >> 1] = pack_bf16(ex2(fmaf(__uint_as_float(sv[k]), sl2, -l4.x)),
+                           ex2(fmaf(__uint_as_float(sv[k + 1]), sl2, -l4.y)));
+    pk[(k >> 1) + 1] = pack_bf16(ex2(fmaf(__uint_as_float(sv[k + 2]), sl2, -l4.z)),
+                                 ex2(fmaf(__uint_as_float(sv[k + 3]), sl2, -l4.w)));
+  }
+}
+
+// dS^T = P^T (dP^T - Delta) for N columns starting at query column qb; P^T
+// packed bf16 in pk, result packed into dd.
+template <int N>
+__device__ __forceinline__ void ds_chunk_bwd(const uint32_t* pk, const uint32_t* dp, uint32_t* dd, const int qb,
+                                             const float* lv) {
+#pragma unroll
+  for (int k = 0; k < N; k += 4) {
+    const float4 d4 = *reinterpret_cast<const float4*>(&lv[128 + qb + k]);
+    const uint32_t a = pk[k >> 1], b = pk[(k >> 1) + 1];
+    dd[k >> 1] = pack_bf16(__uint_as_float(a << 16) * (__uint_as_float(dp[k]) - d4.x),
+                           __uint_as_float(a & 0xffff0000u) * (__uint_as_float(dp[k + 1]) - d4.y));
+    dd[(k >> 1) + 1] = pack_bf16(__uint_as_float(b << 16) * (__uint_as_float(dp[k + 2]) - d4.z),
+                                 __uint_as_float(b & 0xffff0000u) * (__uint_as_float(dp[k + 3]) - d4.w));
+  }
+}
+
+// Store QH/2 packed columns (16 or 24) of this warp's lanes.
+template <int NP>
+__device__ __forceinline__ void tmem_st_packed(uint32_t taddr, const uint32_t* r) {
+  tmem_st16(taddr, r);
+  if constexpr (NP == 24) tmem_st8(taddr + 16, r + 16);
+}
+
+// dR_k of head h from the accumulator columns (minus the earlier heads' share).
+template <int RP>
+__device__ __forceinline__ void store_drk(const BwdParams& p, const SeqInfo& si, int h, int64_t krow, bool kv_valid,
+                                          uint32_t tcol, const float* drk_prev, uint32_t* rv) {
+  const ProblemDev& P = p.prob;
+  const float gsh = __ldg(P.gs + h);  // dR_k = gs * dS^T R_q
+  if (RP == 16) {
+    tmem_ld16(tcol, rv);
+    tmem_ld_wait16(rv);
+  } else {
+    tmem_ld32(tcol, rv);
+    tmem_ld_wait32(rv);
+  }
+  if (kv_valid) {
+    __nv_bfloat16* dst = p.drk + si.b * p.drk_sb + h * p.drk_sh + krow * p.drk_sr;
+#pragma unroll
+    for (int c = 0; c < RP; c += 8) {
+      if (c < P.rank) {
+        uint4 w;
+        uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          wp[i] = pack_bf16((__uint_as_float(rv[c + 2 * i]) - drk_prev[c + 2 * i]) * gsh,
+                            (__uint_as_float(rv[c + 2 * i + 1]) - drk_prev[c + 2 * i + 1]) * gsh);
+        *reinterpret_cast<uint4*>(dst + c) = w;
+      }
     }
   }
 }
@@ -240,6 +305,8 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
                          const __grid_constant__ CUtensorMap tmRq, const __grid_constant__ CUtensorMap tmRk,
                          const BwdParams p) {
   using L = DkdvSmem<D, RP>;
+  using C = DkdvCfg<D, RP>;
+  constexpr int QT = C::QT, QH = C::QH;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::oBar);
@@ -255,9 +322,9 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
   if (n0 >= si.len_k) return;
   const int g = P.heads / P.heads_kv;
   const int gh = max(0, min(g, P.heads_graph - hk * g));  // graph heads of this group (a prefix)
-  // causal: query tile m sees key rows [n0, n0+128) iff 112*m + 111 >= n0
-  const int m_start = P.causal ? n0 / kQT : 0;
-  const int m_end = (si.len_q + kQT - 1) / kQT;
+  // causal: query tile m sees key rows [n0, n0+128) iff QT*m + QT-1 >= n0
+  const int m_start = P.causal ? n0 / QT : 0;
+  const int m_end = (si.len_q + QT - 1) / QT;
   const int n_it = max(0, m_end - m_start);
   const int total_it = g * n_it;
   const int warp = warp_id();
@@ -284,12 +351,17 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars[kAQFull + s], 1);
       mbar_init(&bars[kAQEmpty + s], 1);
+      mbar_init(&bars[kADoFull + s], 1);
+      mbar_init(&bars[kADoEmpty + s], 1);
       mbar_init(&bars[kAPrep + s], 32);
     }
     mbar_init(&bars[kASFull], 1);
     mbar_init(&bars[kADPFull], 1);
-    mbar_init(&bars[kAPReady], 256);
-    mbar_init(&bars[kADsReady], 256);
+    mbar_init(&bars[kASRead], 8);
+    mbar_init(&bars[kAPReady], 8);
+    mbar_init(&bars[kADsReady], 8);
+    mbar_init(&bars[kADvDone], 1);
+    mbar_init(&bars[kADkDone], 1);
     mbar_init(&bars[kAHeadDone], 1);
     mbar_init(&bars[kAAllDone], 1);
     mbar_init(&bars[kARkReady], 32);
@@ -304,9 +376,8 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tDV = tmem + 0, tDK = tmem + 128, tS = tmem + 288, tDP = tmem + 400;
-  // TMEM column of the packed bf16 operand for the 16 query rows of k-step kk
-  auto packed_col = [](int kk) { return (kk < 4 ? 0 : 64) + (kk & 3) * 8; };
+  const uint32_t tDV = tmem + C::tDV, tDK = tmem + C::tDK, tS = tmem + C::tS, tDP = tmem + C::tDP,
+                 tPT = tmem + C::tPT;
   auto graph_of = [&](int it) { return it / n_it < gh; };
 
   if (warp == 8) {
@@ -333,20 +404,27 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
         }
         for (int mi = 0; mi < n_it; ++mi, ++it) {
           const int s = it & 1;
-          if (it >= 2 && !mbar_wait(&bars[kAQEmpty + s], ((it >> 1) - 1) & 1, abort_flag, 402)) {
+          const uint32_t par = ((it >> 1) - 1) & 1;
+          if (it >= 2 && !mbar_wait(&bars[kAQEmpty + s], par, abort_flag, 402)) {
             ok = false;
             break;
           }
-          const int qrow = si.q_start + (m_start + mi) * kQT;
+          const int qrow = si.q_start + (m_start + mi) * QT;
           uint8_t* sq = smem + (s ? L::oQ1 : L::oQ0);
           uint8_t* sdo = smem + (s ? L::oDo1 : L::oDo0);
-          mbar_expect_tx(&bars[kAQFull + s], 2 * (D / 64) * L::kQChunk + (graph ? L::kQChunk : 0));
+          mbar_expect_tx(&bars[kAQFull + s], (D / 64) * L::kQChunk + (graph ? L::kQChunk : 0));
 #pragma unroll
-          for (int c = 0; c < D / 64; ++c) {
+          for (int c = 0; c < D / 64; ++c)
             tma_load_4d(sq + c * L::kQChunk, &tmQ, &bars[kAQFull + s], c * 64, qrow, h, si.b);
-            tma_load_4d(sdo + c * L::kQChunk, &tmDo, &bars[kAQFull + s], c * 64, qrow, h, si.b);
-          }
           if (graph) tma_load_4d(sq + (D / 64) * L::kQChunk, &tmRq, &bars[kAQFull + s], 0, qrow, h, si.b);
+          if (it >= 2 && !mbar_wait(&bars[kADoEmpty + s], par, abort_flag, 403)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&bars[kADoFull + s], (D / 64) * L::kQChunk);
+#pragma unroll
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_4d(sdo + c * L::kQChunk, &tmDo, &bars[kADoFull + s], c * 64, qrow, h, si.b);
         }
       }
     }
@@ -356,11 +434,11 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
     auto fetch = [&](int it, float (&l2)[4], float (&dl)[4]) {
       const int e = it / n_it, mi = it % n_it;
       const int64_t wbase = (static_cast<int64_t>(si.b) * P.heads + hk * g + e) * p.ws_sbh + si.q_start;
-      const int m0 = (m_start + mi) * kQT;
+      const int m0 = (m_start + mi) * QT;
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int t = lane + 32 * u;
-        const bool valid = t < kQT && m0 + t < si.len_q;
+        const bool valid = t < QT && m0 + t < si.len_q;
         l2[u] = valid ? __ldg(p.ws_lse2 + wbase + m0 + t) : 0.f;
         dl[u] = valid ? __ldg(p.ws_delta + wbase + m0 + t) : 0.f;
       }
@@ -384,6 +462,7 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
         mbar_arrive(&bars[kARkReady]);
       }
       if (it + 1 < total_it) fetch(it + 1, nl2, ndl);
+      // the Q load of tile it implies the stage's previous readers (tile it-2) are done
       if (!mbar_wait(&bars[kAQFull + s], (it >> 1) & 1, abort_flag, 601)) {
         ok = false;
         break;
@@ -402,27 +481,22 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
       }
     }
   } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------ MMA stream 1: S^T, dP^T
     if (lane == 0) {
-      constexpr uint32_t idesc_st = make_idesc_bf16(128, kQT, 0, 0);      // S^T, dP^T (N = 112 queries)
-      constexpr uint32_t idesc_dv = make_idesc_bf16(128, D, 0, 1);        // dV (A in TMEM, B MN-major)
-      constexpr uint32_t idesc_dk = make_idesc_bf16(128, D, 0, 1);        // dK only (vanilla heads)
-      constexpr uint32_t idesc_dkr = make_idesc_bf16(128, D + RP, 0, 1);  // [dK | dR_k]
+      constexpr uint32_t idesc_st = make_idesc_bf16(128, QT, 0, 0);  // S^T, dP^T (N = QT queries)
       const uint32_t r_layout = r_layout_of(RP);
       const uint32_t r_sbo = 8 * RP * 2;
       const uint32_t sK = smem_u32(smem + L::oK), sV = smem_u32(smem + L::oV), sRk = smem_u32(smem + L::oRk);
       auto stage_q = [&](int it) { return smem_u32(smem + ((it & 1) ? L::oQ1 : L::oQ0)); };
       auto stage_do = [&](int it) { return smem_u32(smem + ((it & 1) ? L::oDo1 : L::oDo0)); };
-      auto wait_stage = [&](int it) -> bool {
+      auto issue_s = [&](int it) -> bool {  // S^T = K Q^T (+ R~_k R_q^T)
         const int s = it & 1;
-        if (!mbar_wait(&bars[kAQFull + s], (it >> 1) & 1, abort_flag, 503)) return false;
-        if (!mbar_wait(&bars[kAPrep + s], (it >> 1) & 1, abort_flag, 504)) return false;
-        if (graph_of(it) && (it % n_it) == 0 && !mbar_wait(&bars[kARkReady], (it / n_it) & 1, abort_flag, 502))
+        if (!mbar_wait_spin(&bars[kAQFull + s], (it >> 1) & 1, abort_flag, 503)) return false;
+        if (!mbar_wait_spin(&bars[kAPrep + s], (it >> 1) & 1, abort_flag, 504)) return false;
+        if (graph_of(it) && (it % n_it) == 0 &&
+            !mbar_wait_spin(&bars[kARkReady], (it / n_it) & 1, abort_flag, 502))
           return false;
         tc_fence_after();
-        return true;
-      };
-      auto issue_s = [&](int it) {  // S^T = K Q^T (+ R~_k R_q^T)
         const uint32_t sQ = stage_q(it);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
@@ -437,63 +511,76 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
           if ((it % n_it) == n_it - 1) mma_commit(&bars[kARkEmpty]);  // last use of this head's R_k
         }
         mma_commit(&bars[kASFull]);
+        return true;
       };
-      auto issue_dp = [&](int it) {  // dP^T = V dO^T
+      auto issue_dp = [&](int it) -> bool {  // dP^T = V dO^T
+        if (!mbar_wait_spin(&bars[kADoFull + (it & 1)], (it >> 1) & 1, abort_flag, 505)) return false;
+        tc_fence_after();
         const uint32_t sDo = stage_do(it);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
           mma_ss(tDP, make_sdesc(sV + (kk >> 2) * L::kKChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B),
                  make_sdesc(sDo + (kk >> 2) * L::kQChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B), idesc_st, kk > 0);
         mma_commit(&bars[kADPFull]);
+        return true;
       };
-
-      bool ok = mbar_wait(&bars[kAKV], 0, abort_flag, 501) && wait_stage(0);
-      if (ok) {
-        issue_s(0);
-        issue_dp(0);
+      bool ok = mbar_wait(&bars[kAKV], 0, abort_flag, 501) && issue_s(0) && issue_dp(0);
+      for (int it = 0; ok && it + 1 < total_it; ++it) {
+        // the next S^T as soon as the warps have read this one
+        if (!mbar_wait_spin(&bars[kASRead], it & 1, abort_flag, 510) || !issue_s(it + 1)) break;
+        // the next dP^T once dK has consumed the dS^T packed in the dP^T columns
+        if (!mbar_wait_spin(&bars[kADkDone], it & 1, abort_flag, 511) || !issue_dp(it + 1)) break;
       }
+    }
+  } else if (warp == 11) {
+    // ------------------------------------------------------------ MMA stream 2: dV, dK
+    if (lane == 0) {
+      constexpr uint32_t idesc_dv = make_idesc_bf16(128, D, 0, 1);        // dV (A in TMEM, B MN-major)
+      constexpr uint32_t idesc_dk = make_idesc_bf16(128, D, 0, 1);        // dK only (vanilla heads)
+      constexpr uint32_t idesc_dkr = make_idesc_bf16(128, D + RP, 0, 1);  // [dK | dR_k]
+      auto stage_q = [&](int it) { return smem_u32(smem + ((it & 1) ? L::oQ1 : L::oQ0)); };
+      auto stage_do = [&](int it) { return smem_u32(smem + ((it & 1) ? L::oDo1 : L::oDo0)); };
+      // TMEM column of the packed dS^T for the 16 query rows of k-step kk
+      auto ds_col = [](int kk) { return kk < QH / 16 ? 8 * kk : QH + 8 * (kk - QH / 16); };
+      bool ok = true;
       for (int it = 0; ok && it < total_it; ++it) {
         const bool graph = graph_of(it);
-        // dV += P^T dO   (K = 112 query rows, 7 steps of 16)
-        if (!mbar_wait(&bars[kAPReady], it & 1, abort_flag, 506)) break;
+        // dV += P^T dO   (K = QT query rows)
+        if (!mbar_wait_spin(&bars[kAPReady], it & 1, abort_flag, 506)) break;
         tc_fence_after();
         const uint32_t sDo = stage_do(it), sQ = stage_q(it);
 #pragma unroll
-        for (int kk = 0; kk < kQT / 16; ++kk)
-          mma_ts(tDV, tS + packed_col(kk), make_sdesc(sDo + kk * 2048, L::kQChunk, 1024, kSwizzle128B), idesc_dv,
+        for (int kk = 0; kk < QT / 16; ++kk)
+          mma_ts(tDV, tPT + 8 * kk, make_sdesc(sDo + kk * 2048, L::kQChunk, 1024, kSwizzle128B), idesc_dv,
                  (it > 0 || kk > 0) ? 1u : 0u);
-        // next tile's S^T overlaps the warps' dS^T work (P^T above was read in order;
-        // the stage was loaded while the previous tile ran)
-        if (it + 1 < total_it) {
-          if (!wait_stage(it + 1)) break;
-          issue_s(it + 1);
-        }
+        mma_commit(&bars[kADvDone]);
+        mma_commit(&bars[kADoEmpty + (it & 1)]);
         // [dK | dR_k] += dS^T [Q | R_q]
-        if (!mbar_wait(&bars[kADsReady], it & 1, abort_flag, 507)) break;
+        if (!mbar_wait_spin(&bars[kADsReady], it & 1, abort_flag, 507)) break;
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < kQT / 16; ++kk)
-          mma_ts(tDK, tDP + packed_col(kk), make_sdesc(sQ + kk * 2048, L::kQChunk, 1024, kSwizzle128B),
+        for (int kk = 0; kk < QT / 16; ++kk)
+          mma_ts(tDK, tDP + ds_col(kk), make_sdesc(sQ + kk * 2048, L::kQChunk, 1024, kSwizzle128B),
                  graph ? idesc_dkr : idesc_dk, (it > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&bars[kADkDone]);
         mma_commit(&bars[kAQEmpty + (it & 1)]);
         if (graph && (it % n_it) == n_it - 1 && it + 1 < total_it) mma_commit(&bars[kAHeadDone]);
-        // next tile's dP^T overlaps the warps' next P^T work (dS^T above was read in order)
-        if (it + 1 < total_it) issue_dp(it + 1);
       }
       if (ok) mma_commit(&bars[kAAllDone]);
     }
   } else {
     // ------------------------------------------------------------ softmax-gradient warps 0-7
-    const int wg = warp >> 2;  // warpgroup: query columns [64*wg, min(64*wg+64, 112))
+    const int wg = warp >> 2;  // warpgroup: query columns [QH*wg, QH*wg + QH)
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int t = tid & 127;   // key row within the tile (TMEM lane)
     const int kv_local = n0 + t;
     const bool kv_valid = kv_local < si.len_k;
     const float sl2 = P.scale_log2;
     const int64_t krow = si.k_start + kv_local;
-    const uint32_t tSw = tS + lane_base + 64 * wg, tDPw = tDP + lane_base + 64 * wg;
-    constexpr int kW1 = kQT - 64;  // columns owned by warpgroup 1
-    float drk_prev[RP];                       // dR_k columns already stored for earlier heads
+    const uint32_t tSw = tS + lane_base + QH * wg, tDPw = tDP + lane_base + QH * wg;
+    const uint32_t tPTw = tPT + lane_base + (QH / 2) * wg;
+    const int qw = QH * wg;  // first query column of this warpgroup
+    float drk_prev[RP];      // dR_k columns already stored for earlier heads
 #pragma unroll
     for (int i = 0; i < RP; ++i) drk_prev[i] = 0.f;
     int it = 0, hb = 0;
@@ -504,10 +591,10 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
       const bool graph = e < gh;
       for (int mi = 0; mi < n_it; ++mi, ++it) {
         const int s = it & 1;
-        const int m0 = (m_start + mi) * kQT;
+        const int m0 = (m_start + mi) * QT;
         const float* lv = vec + s * 256;
         // valid query columns q in [q_lo, q_hi) (tile-relative) for this key row
-        const int q_hi = kv_valid ? min(kQT, si.len_q - m0) : 0;
+        const int q_hi = kv_valid ? min(QT, si.len_q - m0) : 0;
         const int q_lo = P.causal ? (kv_local - m0) : 0;
         if (!mbar_wait(&bars[kAPrep + s], (it >> 1) & 1, abort_flag, 702) ||
             !mbar_wait(&bars[kASFull], it & 1, abort_flag, 701)) {
@@ -515,69 +602,48 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
           break;
         }
         tc_fence_after();
-        // phase 1: P^T (packed bf16, kept in registers for phase 2)
-        uint32_t pk[32];
-        {
-          uint32_t sv[32];
-          tmem_ld32(tSw, sv);
-          tmem_ld_wait32(sv);
-          p_chunk_bwd(sv, pk, 0, 64 * wg, 32, q_lo, q_hi, lv, sl2);
-          if (wg == 0) {
-            tmem_ld32(tSw + 32, sv);
-            tmem_ld_wait32(sv);
-            p_chunk_bwd(sv, pk, 16, 32, 32, q_lo, q_hi, lv, sl2);
-          } else {
-            tmem_ld16(tSw + 32, sv);
-            tmem_ld_wait16(sv);
-            p_chunk_bwd(sv, pk, 16, 96, kW1 - 32, q_lo, q_hi, lv, sl2);
-          }
+        // phase 1: read S^T, release it for the next tile, then P^T (packed bf16)
+        uint32_t sv[QH];
+        tmem_ld32(tSw, sv);
+        if constexpr (QH == 48) tmem_ld16(tSw + 32, sv + 32);
+        tmem_ld_wait32(sv);
+        if constexpr (QH == 48) tmem_ld_wait16(sv + 32);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[kASRead]);
+        uint32_t pk[QH / 2];
+        p_chunk_bwd<32>(sv, pk, qw, q_lo, q_hi, lv, sl2);
+        if constexpr (QH == 48) p_chunk_bwd<16>(sv + 32, pk + 16, qw + 32, q_lo, q_hi, lv, sl2);
+        // the P^T columns are free once the previous tile's dV has run
+        if (it > 0 && !mbar_wait(&bars[kADvDone], (it - 1) & 1, abort_flag, 703)) {
+          ok = false;
+          break;
         }
-        tmem_st32(tSw, pk);  // columns this warpgroup has already read (16 unused by warpgroup 1)
+        tc_fence_after();
+        tmem_st_packed<QH / 2>(tPTw, pk);
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&bars[kAPReady]);
-        // phase 2: dS^T = P^T (dP^T - Delta)
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[kAPReady]);
+        // phase 2: dS^T = P^T (dP^T - Delta) into the first half of this warpgroup's dP^T columns
         if (!mbar_wait(&bars[kADPFull], it & 1, abort_flag, 704)) {
           ok = false;
           break;
         }
         tc_fence_after();
         {
-          uint32_t dp[32], dd[32];
+          uint32_t dp[QH], dd[QH / 2];
           tmem_ld32(tDPw, dp);
+          if constexpr (QH == 48) tmem_ld16(tDPw + 32, dp + 32);
           tmem_ld_wait32(dp);
-#pragma unroll
-          for (int k = 0; k < 32; k += 4) {
-            const float4 d4 = *reinterpret_cast<const float4*>(&lv[128 + 64 * wg + k]);
-            const uint32_t a = pk[k >> 1], b = pk[(k >> 1) + 1];
-            dd[k >> 1] = pack_bf16(__uint_as_float(a << 16) * (__uint_as_float(dp[k]) - d4.x),
-                                   __uint_as_float(a & 0xffff0000u) * (__uint_as_float(dp[k + 1]) - d4.y));
-            dd[(k >> 1) + 1] = pack_bf16(__uint_as_float(b << 16) * (__uint_as_float(dp[k + 2]) - d4.z),
-                                         __uint_as_float(b & 0xffff0000u) * (__uint_as_float(dp[k + 3]) - d4.w));
-          }
-          if (wg == 0) {
-            tmem_ld32(tDPw + 32, dp);
-            tmem_ld_wait32(dp);
-          } else {
-            tmem_ld16(tDPw + 32, dp);
-            tmem_ld_wait16(dp);
-#pragma unroll
-            for (int k = 16; k < 32; ++k) dp[k] = 0u;  // beyond the 112-column tile
-          }
-#pragma unroll
-          for (int k = 0; k < 32; k += 4) {
-            const float4 d4 = *reinterpret_cast<const float4*>(&lv[128 + 64 * wg + 32 + k]);
-            const uint32_t a = pk[16 + (k >> 1)], b = pk[16 + (k >> 1) + 1];
-            dd[16 + (k >> 1)] = pack_bf16(__uint_as_float(a << 16) * (__uint_as_float(dp[k]) - d4.x),
-                                          __uint_as_float(a & 0xffff0000u) * (__uint_as_float(dp[k + 1]) - d4.y));
-            dd[16 + (k >> 1) + 1] = pack_bf16(__uint_as_float(b << 16) * (__uint_as_float(dp[k + 2]) - d4.z),
-                                              __uint_as_float(b & 0xffff0000u) * (__uint_as_float(dp[k + 3]) - d4.w));
-          }
-          tmem_st32(tDPw, dd);
+          if constexpr (QH == 48) tmem_ld_wait16(dp + 32);
+          ds_chunk_bwd<QH>(pk, dp, dd, qw, lv);
+          tmem_st_packed<QH / 2>(tDPw, dd);
         }
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&bars[kADsReady]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[kADsReady]);
         // GQA: at the end of a graph head that is followed by another head, store
         // this head's dR_k columns (accumulated on top of the earlier heads')
         if (wg == 0 && graph && mi == n_it - 1 && it + 1 < total_it) {
@@ -587,30 +653,8 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
           }
           ++hb;
           tc_fence_after();
-          const float gsh = __ldg(P.gs + h);  // dR_k = gs * dS^T R_q
           uint32_t rv[32];
-          if (RP == 16) {
-            tmem_ld16(tDK + lane_base + D, rv);
-            tmem_ld_wait16(rv);
-          } else {
-            tmem_ld32(tDK + lane_base + D, rv);
-            tmem_ld_wait32(rv);
-          }
-          if (kv_valid) {
-            __nv_bfloat16* dst = p.drk + si.b * p.drk_sb + h * p.drk_sh + krow * p.drk_sr;
-#pragma unroll
-            for (int c = 0; c < RP; c += 8) {
-              if (c < P.rank) {
-                uint4 w;
-                uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                  wp[i] = pack_bf16((__uint_as_float(rv[c + 2 * i]) - drk_prev[c + 2 * i]) * gsh,
-                                    (__uint_as_float(rv[c + 2 * i + 1]) - drk_prev[c + 2 * i + 1]) * gsh);
-                *reinterpret_cast<uint4*>(dst + c) = w;
-              }
-            }
-          }
+          store_drk<RP>(p, si, h, krow, kv_valid, tDK + lane_base + D, drk_prev, rv);
 #pragma unroll
           for (int i = 0; i < RP; ++i) drk_prev[i] = __uint_as_float(rv[i]);
         }
@@ -634,31 +678,8 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
       }
       if (wg == 0 && gh > 0 && gh == g) {
         // dR_k of the group's last head (a graph head; otherwise it was stored at its end)
-        const int h = hk * g + gh - 1;
-        const float gsh = __ldg(P.gs + h);  // dR_k = gs * dS^T R_q
         uint32_t rv[32];
-        if (RP == 16) {
-          tmem_ld16(tDK + lane_base + D, rv);
-          tmem_ld_wait16(rv);
-        } else {
-          tmem_ld32(tDK + lane_base + D, rv);
-          tmem_ld_wait32(rv);
-        }
-        if (kv_valid) {
-          __nv_bfloat16* dst = p.drk + si.b * p.drk_sb + h * p.drk_sh + krow * p.drk_sr;
-#pragma unroll
-          for (int c = 0; c < RP; c += 8) {
-            if (c < P.rank) {
-              uint4 w;
-              uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
-#pragma unroll
-              for (int i = 0; i < 4; ++i)
-                wp[i] = pack_bf16((__uint_as_float(rv[c + 2 * i]) - drk_prev[c + 2 * i]) * gsh,
-                                  (__uint_as_float(rv[c + 2 * i + 1]) - drk_prev[c + 2 * i + 1]) * gsh);
-              *reinterpret_cast<uint4*>(dst + c) = w;
-            }
-          }
-        }
+        store_drk<RP>(p, si, hk * g + gh - 1, krow, kv_valid, tDK + lane_base + D, drk_prev, rv);
       }
     }
   }
@@ -671,6 +692,8 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
   }
 }
 
+constexpr int kQT = 112;  // key rows per tile of the query-stationary (dQ) kernel
+
 // ---------------------------------------------------------------------------
 // dQ / dR_q / d_gs  (Q-stationary)
 // ---------------------------------------------------------------------------
@@ -678,10 +701,11 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
 // visible 112-row key tiles.  The stationary Q and dO tiles live in tensor
 // memory (A operands of the S and dP MMAs in the TS form), which leaves shared
 // memory for three-deep K and V rings.  They arrive by TMA in the V ring
-// (before its first use) and are moved to tensor memory by tcgen05.cp.  dR_q rides along with dQ as extra
-// accumulator columns: the B operand of the dQ MMA is [K | R_k] (R_k as a
-// zero-padded third 64-column swizzle atom next to K's two), so one
-// N = D + r_pad MMA per k-step yields dQ and dS R_k together.
+// (before its first use) and are moved to tensor memory by tcgen05.cp.
+// dR_q rides along with dQ as extra accumulator columns: the B operand of the
+// dQ MMA is [K | R_k] (R_k as a zero-padded third 64-column swizzle atom next
+// to K's two), so one N = D + r_pad MMA per k-step yields dQ and dS R_k
+// together.
 // TMEM columns: [dQ | dS R_k] [0,160) S [160,272) dP [272,384) Q [384,448)
 // dO [448,512).
 // Key tiles are visited from the diagonal down to the first one: the CTAs of
@@ -1125,7 +1149,7 @@ cudaError_t launch_bwd_t(const BwdMaps& m, const BwdParams& p, cudaStream_t stre
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
     if (e != cudaSuccess) return e;
     dim3 grid(p.n_nblocks, p.prob.heads_kv, p.batch);
-    kern<<<grid, kDkdvThreads, L::kTotal, stream>>>(m.q112, m.k, m.v, m.dO112, m.rq112, m.rk, p);
+    kern<<<grid, kDkdvThreads, L::kTotal, stream>>>(m.qS, m.k, m.v, m.dOS, m.rqS, m.rk, p);
     e = cudaGetLastError();
     if (e == cudaSuccess && ev) e = cudaEventRecord(ev[2], stream);
     if (e != cudaSuccess) return e;

@@ -13,6 +13,11 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kEps = 1e-6f;  // O = acc/(l+1e-6), LSE = m + log(l+1e-6)  (flash_naylis_attn.py:192,195)
 
+// Query rows per tile of the key-stationary backward kernel: the largest
+// multiple of 32 for which dV, [dK | dR_k], S^T, dP^T and a separate packed
+// P^T fit in the 512 TMEM columns.
+__host__ __device__ constexpr int dkdv_query_rows(int D, int RP) { return (D == 128 && RP == 32) ? 64 : 96; }
+
 // Sequence bounds of one (batch or packed sequence) index. Dense problems have
 // all sequences of length seqlen_q/seqlen_k starting at row 0 of their batch.
 struct SeqInfo {
@@ -95,12 +100,12 @@ struct BwdParams {
 };
 
 // Tensor maps of one backward call.  Each kernel tiles its stationary operand
-// by 128 rows and the streamed one by 112 rows; the streamed R operand is read
-// as a zero-padded 64-column swizzle atom next to Q (dK/dV) or K (dQ).
+// by 128 rows and streams the other in smaller tiles; the streamed R operand
+// is read as a zero-padded 64-column swizzle atom next to Q (dK/dV) or K (dQ).
 struct BwdMaps {
-  CUtensorMap q, k, v, dO, rq, rk;        // 128-row boxes (R with r_pad-column boxes)
-  CUtensorMap q112, dO112, rq112;         // streamed by the key-stationary kernel
-  CUtensorMap k112, v112, rk112;          // streamed by the query-stationary kernel
+  CUtensorMap q, k, v, dO, rq, rk;  // 128-row boxes (R with r_pad-column boxes)
+  CUtensorMap qS, dOS, rqS;         // dkdv_query_rows-row boxes, streamed by the key-stationary kernel
+  CUtensorMap k112, v112, rk112;    // 112-row boxes, streamed by the query-stationary kernel
 };
 
 }  // namespace fna2

@@ -117,32 +117,33 @@ extern "C" int fna2_bwd_noalloc(const Fna2BwdArgs* a, void* stream) {
     return noalloc_map(m, t.ptr, s.r, rows, s.HG, s.batch_dim(), t.stride[2], t.stride[1], t.stride[0], s.RP, 128,
                        s.RP == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B, what);
   };
-  auto map_t112 = [&](CUtensorMap* m, const Fna2Tensor& t, int rows, int heads, const char* what) {
-    return noalloc_map(m, t.ptr, s.D, rows, heads, s.batch_dim(), t.stride[2], t.stride[1], t.stride[0], 64, kQT,
-                       CU_TENSOR_MAP_SWIZZLE_128B, what);
+  auto map_tt = [&](CUtensorMap* m, const Fna2Tensor& t, int rows, int heads, int box_rows, const char* what) {
+    return noalloc_map(m, t.ptr, s.D, rows, heads, s.batch_dim(), t.stride[2], t.stride[1], t.stride[0], 64,
+                       box_rows, CU_TENSOR_MAP_SWIZZLE_128B, what);
   };
-  auto map_rr112 = [&](CUtensorMap* m, const Fna2Tensor& t, int rows, const char* what) {
-    return noalloc_map(m, t.ptr, s.r, rows, s.HG, s.batch_dim(), t.stride[2], t.stride[1], t.stride[0], 64, kQT,
-                       CU_TENSOR_MAP_SWIZZLE_128B, what);
+  auto map_rt = [&](CUtensorMap* m, const Fna2Tensor& t, int rows, int box_rows, const char* what) {
+    return noalloc_map(m, t.ptr, s.r, rows, s.HG, s.batch_dim(), t.stride[2], t.stride[1], t.stride[0], 64,
+                       box_rows, CU_TENSOR_MAP_SWIZZLE_128B, what);
   };
+  const int qs_rows = dkdv_query_rows(s.D, s.RP);
   BwdMaps mp;
   if (int rc = map_t(&mp.q, a->q, s.rows_q(), s.H, "q")) return rc;
   if (int rc = map_t(&mp.k, a->k, s.rows_k(), s.HKV, "k")) return rc;
   if (int rc = map_t(&mp.v, a->v, s.rows_k(), s.HKV, "v")) return rc;
   if (int rc = map_t(&mp.dO, a->dout, s.rows_q(), s.H, "dout")) return rc;
-  if (int rc = map_t112(&mp.q112, a->q, s.rows_q(), s.H, "q")) return rc;
-  if (int rc = map_t112(&mp.dO112, a->dout, s.rows_q(), s.H, "dout")) return rc;
-  if (int rc = map_t112(&mp.k112, a->k, s.rows_k(), s.HKV, "k")) return rc;
-  if (int rc = map_t112(&mp.v112, a->v, s.rows_k(), s.HKV, "v")) return rc;
+  if (int rc = map_tt(&mp.qS, a->q, s.rows_q(), s.H, qs_rows, "q")) return rc;
+  if (int rc = map_tt(&mp.dOS, a->dout, s.rows_q(), s.H, qs_rows, "dout")) return rc;
+  if (int rc = map_tt(&mp.k112, a->k, s.rows_k(), s.HKV, kQT, "k")) return rc;
+  if (int rc = map_tt(&mp.v112, a->v, s.rows_k(), s.HKV, kQT, "v")) return rc;
   if (s.HG > 0) {
     if (int rc = map_rr(&mp.rq, a->r_q, s.rows_q(), "r_q")) return rc;
     if (int rc = map_rr(&mp.rk, a->r_k, s.rows_k(), "r_k")) return rc;
-    if (int rc = map_rr112(&mp.rq112, a->r_q, s.rows_q(), "r_q")) return rc;
-    if (int rc = map_rr112(&mp.rk112, a->r_k, s.rows_k(), "r_k")) return rc;
+    if (int rc = map_rt(&mp.rqS, a->r_q, s.rows_q(), qs_rows, "r_q")) return rc;
+    if (int rc = map_rt(&mp.rk112, a->r_k, s.rows_k(), kQT, "r_k")) return rc;
   } else {
     mp.rq = mp.q;
     mp.rk = mp.k;
-    mp.rq112 = mp.q112;
+    mp.rqS = mp.qS;
     mp.rk112 = mp.k112;
   }
   BwdParams p;
