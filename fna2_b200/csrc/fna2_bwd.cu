@@ -151,18 +151,19 @@ __device__ __forceinline__ uint32_t r_layout_of(int rp) {
 // per k-step yields dK and dS^T R_q (dR_k = gs * that).
 //
 // TMEM columns: dV [0,D) | dK,dR_k [D,2D+r_pad) | S^T (QT) | dP^T (QT) | P^T
-// (QT/2, packed bf16).  P^T has its own columns so that the next tile's S^T
-// can be computed as soon as the warps have read S^T; dS^T is packed into
-// the first half of each warpgroup's own dP^T columns.
+// then dS^T (QT/2, packed bf16).  With the packed operands in their own
+// columns, the next tile's S^T and dP^T can be computed as soon as the warps
+// have read this tile's S^T and dP^T.  P^T and dS^T share their columns: dS^T
+// is written once dV has read P^T, the next P^T once dK has read dS^T.
 // Per query tile (warpgroup w owns query columns [w*QT/2, (w+1)*QT/2), each
 // thread one key row = TMEM lane):
 //   tensor core:  S^T = K Q^T (+ R~_k R_q^T), dP^T = V dO^T  (SS)
 //   warps:        P^T = exp2(S^T*c - LSE2) (bf16), dS^T = P^T (dP^T - Delta)
 //   tensor core:  dV += P^T dO, [dK | dR_k] += dS^T [Q | R_q]  (TS form)
-// Two threads issue MMAs: one the S^T and dP^T groups, the other the dV and
-// dK groups, so that neither waits on a barrier behind its own queued MMAs
-// while the other's are executing.  The only cross-stream hazard, dP^T of
-// the next tile overwriting the dS^T that dK reads, is ordered by a barrier.
+// Two threads issue MMAs: one S^T and dP^T, the other dV and dK, so that a
+// barrier wait of one stream never sits behind the other stream's queued
+// MMAs (a thread's wait issued behind its own queued MMAs only returns once
+// the tensor pipe has nearly drained them).
 template <int D, int RP>
 struct DkdvCfg {
   static constexpr int QT = dkdv_query_rows(D, RP);
@@ -184,15 +185,20 @@ struct DkdvSmem {
   static constexpr int oK = 0;
   static constexpr int oV = align(oK + kKTile);
   static constexpr int oRk = align(oV + kKTile);
-  static constexpr int oQ0 = align(oRk + kRk);                 // [Q c0 | (Q c1) | R_q] per stage
-  static constexpr int oQ1 = align(oQ0 + kQAtoms * kQChunk);
-  static constexpr int oDo0 = align(oQ1 + kQAtoms * kQChunk);
-  static constexpr int oDo1 = align(oDo0 + (D / 64) * kQChunk);
-  static constexpr int oVec = align(oDo1 + (D / 64) * kQChunk);  // [2 stages][lse2 128 | delta 128] floats
-  static constexpr int oBar = oVec + 2 * 256 * 4;
-  static constexpr int kNumBars = 24;
+  static constexpr int kQStages = 3;                       // Q ring depth (dO: 2)
+  static constexpr int kQStage = kQAtoms * kQChunk;         // [Q c0 | (Q c1) | R_q]
+  static constexpr int kDoStage = (D / 64) * kQChunk;
+  static constexpr int oQ = align(oRk + kRk);
+  static constexpr int oDo = oQ + kQStages * kQStage;
+  static constexpr int oVec = oDo + 2 * kDoStage;            // per Q stage: [lse2 QT | delta QT] floats
+  static constexpr int oBar = oVec + kQStages * 2 * QT * 4;
+  static constexpr int kNumBars = 27;
   static constexpr int oMisc = oBar + kNumBars * 8;
-  static constexpr int kTotal = oMisc + 16 + 1024;
+  static constexpr int kUsed = oMisc + 16;
+  // 1024 bytes of slack for aligning the base when they fit; otherwise the
+  // kernel checks that the dynamic shared memory base is 1024-byte aligned
+  static constexpr int kTotal = kUsed + 1024 <= kMaxDynamicSmem ? kUsed + 1024 : kUsed;
+  static_assert(kUsed <= kMaxDynamicSmem, "shared memory budget");
   static_assert(kQChunk % 1024 == 0, "swizzle atoms need 1024-byte alignment");
 };
 
@@ -200,21 +206,22 @@ enum DkdvBar {
   kAKV = 0,
   kARkFull = 1,
   kARkEmpty = 2,
-  kAQFull = 3,     // +stage: Q and R_q of a query tile
-  kAQEmpty = 5,    // +stage (last reader: dK)
-  kADoFull = 7,    // +stage: dO of a query tile (loaded behind Q)
-  kADoEmpty = 9,   // +stage (last reader: dV)
-  kAPrep = 11,     // +stage: lse2/Delta rows in shared memory
-  kASFull = 13,
-  kADPFull = 14,
-  kASRead = 15,    // warps have read S^T (one arrival per warp)
-  kAPReady = 16,   // P^T in TMEM (one arrival per warp)
-  kADsReady = 17,  // dS^T in TMEM (one arrival per warp)
-  kADvDone = 18,   // dV MMA of a tile complete (P^T columns free)
-  kADkDone = 19,   // dK MMA of a tile complete (dS^T columns free)
-  kAHeadDone = 20,
-  kAAllDone = 21,
-  kARkReady = 22,  // R~_k scaled in shared memory (once per graph head)
+  kAQFull = 3,     // +stage (3): Q and R_q of a query tile
+  kAQEmpty = 6,    // +stage (3) (last reader: dK)
+  kADoFull = 9,    // +stage (2): dO of a query tile (loaded behind Q)
+  kADoEmpty = 11,  // +stage (2) (readers: dP^T and dV, one arrival each)
+  kAPrep = 13,     // +stage (3): lse2/Delta rows in shared memory
+  kASFull = 16,
+  kADPFull = 17,
+  kASRead = 18,    // warps have read S^T (one arrival per warp)
+  kAPReady = 19,   // P^T in TMEM (one arrival per warp)
+  kADsReady = 20,  // dS^T in TMEM (one arrival per warp)
+  kADvDone = 21,   // dV MMA of a tile complete (P^T columns free)
+  kAHeadDone = 22,
+  kAAllDone = 23,
+  kARkReady = 24,  // R~_k scaled in shared memory (once per graph head)
+  kADpRead = 25,   // warps have read dP^T (one arrival per warp)
+  kADkDone = 26,   // dK MMA of a tile complete (dS^T columns free)
 };
 
 constexpr int kDkdvThreads = 384;  // 8 softmax-gradient warps, producer, MMA (S/dP), prep, MMA (dV/dK)
@@ -249,10 +256,10 @@ __device__ __forceinline__ void p_chunk_bwd(const uint32_t* sv_in, uint32_t* pk,
 // packed bf16 in pk, result packed into dd.
 template <int N>
 __device__ __forceinline__ void ds_chunk_bwd(const uint32_t* pk, const uint32_t* dp, uint32_t* dd, const int qb,
-                                             const float* lv) {
+                                             const float* dv) {
 #pragma unroll
   for (int k = 0; k < N; k += 4) {
-    const float4 d4 = *reinterpret_cast<const float4*>(&lv[128 + qb + k]);
+    const float4 d4 = *reinterpret_cast<const float4*>(&dv[qb + k]);
     const uint32_t a = pk[k >> 1], b = pk[(k >> 1) + 1];
     dd[k >> 1] = pack_bf16(__uint_as_float(a << 16) * (__uint_as_float(dp[k]) - d4.x),
                            __uint_as_float(a & 0xffff0000u) * (__uint_as_float(dp[k + 1]) - d4.y));
@@ -309,6 +316,10 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
   constexpr int QT = C::QT, QH = C::QH;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  if ((smem - smem_raw) + L::kUsed > L::kTotal) {  // layout does not fit the launch's shared memory
+    if (threadIdx.x == 0) atomicCAS(&g_device_error, 0, 499);
+    return;
+  }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::oBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::oMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::oMisc + 4);
@@ -348,12 +359,14 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
     mbar_init(&bars[kAKV], 1);
     mbar_init(&bars[kARkFull], 1);
     mbar_init(&bars[kARkEmpty], 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < L::kQStages; ++s) {
       mbar_init(&bars[kAQFull + s], 1);
       mbar_init(&bars[kAQEmpty + s], 1);
-      mbar_init(&bars[kADoFull + s], 1);
-      mbar_init(&bars[kADoEmpty + s], 1);
       mbar_init(&bars[kAPrep + s], 32);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars[kADoFull + s], 1);
+      mbar_init(&bars[kADoEmpty + s], 2);  // released by dP^T (stream 1) and dV (stream 2)
     }
     mbar_init(&bars[kASFull], 1);
     mbar_init(&bars[kADPFull], 1);
@@ -361,6 +374,7 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
     mbar_init(&bars[kAPReady], 8);
     mbar_init(&bars[kADsReady], 8);
     mbar_init(&bars[kADvDone], 1);
+    mbar_init(&bars[kADpRead], 8);
     mbar_init(&bars[kADkDone], 1);
     mbar_init(&bars[kAHeadDone], 1);
     mbar_init(&bars[kAAllDone], 1);
@@ -403,28 +417,28 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
           tma_load_4d(smem + L::oRk, &tmRk, &bars[kARkFull], 0, krow, h, si.b);
         }
         for (int mi = 0; mi < n_it; ++mi, ++it) {
-          const int s = it & 1;
-          const uint32_t par = ((it >> 1) - 1) & 1;
-          if (it >= 2 && !mbar_wait(&bars[kAQEmpty + s], par, abort_flag, 402)) {
+          const int sq_i = it % L::kQStages, sd = it & 1;
+          if (it >= L::kQStages &&
+              !mbar_wait(&bars[kAQEmpty + sq_i], ((it / L::kQStages) - 1) & 1, abort_flag, 402)) {
             ok = false;
             break;
           }
           const int qrow = si.q_start + (m_start + mi) * QT;
-          uint8_t* sq = smem + (s ? L::oQ1 : L::oQ0);
-          uint8_t* sdo = smem + (s ? L::oDo1 : L::oDo0);
-          mbar_expect_tx(&bars[kAQFull + s], (D / 64) * L::kQChunk + (graph ? L::kQChunk : 0));
+          uint8_t* sq = smem + L::oQ + sq_i * L::kQStage;
+          uint8_t* sdo = smem + L::oDo + sd * L::kDoStage;
+          mbar_expect_tx(&bars[kAQFull + sq_i], (D / 64) * L::kQChunk + (graph ? L::kQChunk : 0));
 #pragma unroll
           for (int c = 0; c < D / 64; ++c)
-            tma_load_4d(sq + c * L::kQChunk, &tmQ, &bars[kAQFull + s], c * 64, qrow, h, si.b);
-          if (graph) tma_load_4d(sq + (D / 64) * L::kQChunk, &tmRq, &bars[kAQFull + s], 0, qrow, h, si.b);
-          if (it >= 2 && !mbar_wait(&bars[kADoEmpty + s], par, abort_flag, 403)) {
+            tma_load_4d(sq + c * L::kQChunk, &tmQ, &bars[kAQFull + sq_i], c * 64, qrow, h, si.b);
+          if (graph) tma_load_4d(sq + (D / 64) * L::kQChunk, &tmRq, &bars[kAQFull + sq_i], 0, qrow, h, si.b);
+          if (it >= 2 && !mbar_wait(&bars[kADoEmpty + sd], ((it >> 1) - 1) & 1, abort_flag, 403)) {
             ok = false;
             break;
           }
-          mbar_expect_tx(&bars[kADoFull + s], (D / 64) * L::kQChunk);
+          mbar_expect_tx(&bars[kADoFull + sd], (D / 64) * L::kQChunk);
 #pragma unroll
           for (int c = 0; c < D / 64; ++c)
-            tma_load_4d(sdo + c * L::kQChunk, &tmDo, &bars[kADoFull + s], c * 64, qrow, h, si.b);
+            tma_load_4d(sdo + c * L::kQChunk, &tmDo, &bars[kADoFull + sd], c * 64, qrow, h, si.b);
         }
       }
     }
@@ -447,7 +461,7 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
     fetch(0, l2, dl);
     bool ok = true;
     for (int it = 0; ok && it < total_it; ++it) {
-      const int s = it & 1;
+      const int s = it % L::kQStages;
       const int e = it / n_it;
       if (e < gh && (it % n_it) == 0) {
         // a new graph head: R~_k = R_k * gs/scale in place (element-wise, any swizzle)
@@ -462,16 +476,18 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
         mbar_arrive(&bars[kARkReady]);
       }
       if (it + 1 < total_it) fetch(it + 1, nl2, ndl);
-      // the Q load of tile it implies the stage's previous readers (tile it-2) are done
-      if (!mbar_wait(&bars[kAQFull + s], (it >> 1) & 1, abort_flag, 601)) {
+      // the Q load of tile it implies the stage's previous readers (tile it-3) are done
+      if (!mbar_wait(&bars[kAQFull + s], (it / L::kQStages) & 1, abort_flag, 601)) {
         ok = false;
         break;
       }
-      float* lv = vec + s * 256;
+      float* lv = vec + s * 2 * QT;
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        lv[lane + 32 * u] = l2[u];
-        lv[128 + lane + 32 * u] = dl[u];
+        if (lane + 32 * u < QT) {
+          lv[lane + 32 * u] = l2[u];
+          lv[QT + lane + 32 * u] = dl[u];
+        }
       }
       mbar_arrive(&bars[kAPrep + s]);
 #pragma unroll
@@ -487,12 +503,12 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
       const uint32_t r_layout = r_layout_of(RP);
       const uint32_t r_sbo = 8 * RP * 2;
       const uint32_t sK = smem_u32(smem + L::oK), sV = smem_u32(smem + L::oV), sRk = smem_u32(smem + L::oRk);
-      auto stage_q = [&](int it) { return smem_u32(smem + ((it & 1) ? L::oQ1 : L::oQ0)); };
-      auto stage_do = [&](int it) { return smem_u32(smem + ((it & 1) ? L::oDo1 : L::oDo0)); };
+      auto stage_q = [&](int it) { return smem_u32(smem + L::oQ + (it % L::kQStages) * L::kQStage); };
       auto issue_s = [&](int it) -> bool {  // S^T = K Q^T (+ R~_k R_q^T)
-        const int s = it & 1;
-        if (!mbar_wait_spin(&bars[kAQFull + s], (it >> 1) & 1, abort_flag, 503)) return false;
-        if (!mbar_wait_spin(&bars[kAPrep + s], (it >> 1) & 1, abort_flag, 504)) return false;
+        const int s = it % L::kQStages;
+        const uint32_t par = (it / L::kQStages) & 1;
+        if (!mbar_wait_spin(&bars[kAQFull + s], par, abort_flag, 503)) return false;
+        if (!mbar_wait_spin(&bars[kAPrep + s], par, abort_flag, 504)) return false;
         if (graph_of(it) && (it % n_it) == 0 &&
             !mbar_wait_spin(&bars[kARkReady], (it / n_it) & 1, abort_flag, 502))
           return false;
@@ -516,21 +532,20 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
       auto issue_dp = [&](int it) -> bool {  // dP^T = V dO^T
         if (!mbar_wait_spin(&bars[kADoFull + (it & 1)], (it >> 1) & 1, abort_flag, 505)) return false;
         tc_fence_after();
-        const uint32_t sDo = stage_do(it);
+        const uint32_t sDo = smem_u32(smem + L::oDo + (it & 1) * L::kDoStage);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
           mma_ss(tDP, make_sdesc(sV + (kk >> 2) * L::kKChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B),
                  make_sdesc(sDo + (kk >> 2) * L::kQChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B), idesc_st, kk > 0);
         mma_commit(&bars[kADPFull]);
+        mma_commit(&bars[kADoEmpty + (it & 1)]);
         return true;
       };
       bool ok = mbar_wait(&bars[kAKV], 0, abort_flag, 501) && issue_s(0) && issue_dp(0);
-      for (int it = 0; ok && it + 1 < total_it; ++it) {
-        // the next S^T as soon as the warps have read this one
-        if (!mbar_wait_spin(&bars[kASRead], it & 1, abort_flag, 510) || !issue_s(it + 1)) break;
-        // the next dP^T once dK has consumed the dS^T packed in the dP^T columns
-        if (!mbar_wait_spin(&bars[kADkDone], it & 1, abort_flag, 511) || !issue_dp(it + 1)) break;
-      }
+      // the next S^T and dP^T as soon as the warps have read this tile's
+      for (int it = 0; ok && it + 1 < total_it; ++it)
+        ok = mbar_wait_spin(&bars[kASRead], it & 1, abort_flag, 510) && issue_s(it + 1) &&
+             mbar_wait_spin(&bars[kADpRead], it & 1, abort_flag, 511) && issue_dp(it + 1);
     }
   } else if (warp == 11) {
     // ------------------------------------------------------------ MMA stream 2: dV, dK
@@ -538,10 +553,8 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
       constexpr uint32_t idesc_dv = make_idesc_bf16(128, D, 0, 1);        // dV (A in TMEM, B MN-major)
       constexpr uint32_t idesc_dk = make_idesc_bf16(128, D, 0, 1);        // dK only (vanilla heads)
       constexpr uint32_t idesc_dkr = make_idesc_bf16(128, D + RP, 0, 1);  // [dK | dR_k]
-      auto stage_q = [&](int it) { return smem_u32(smem + ((it & 1) ? L::oQ1 : L::oQ0)); };
-      auto stage_do = [&](int it) { return smem_u32(smem + ((it & 1) ? L::oDo1 : L::oDo0)); };
-      // TMEM column of the packed dS^T for the 16 query rows of k-step kk
-      auto ds_col = [](int kk) { return kk < QH / 16 ? 8 * kk : QH + 8 * (kk - QH / 16); };
+      auto stage_q = [&](int it) { return smem_u32(smem + L::oQ + (it % L::kQStages) * L::kQStage); };
+      auto stage_do = [&](int it) { return smem_u32(smem + L::oDo + (it & 1) * L::kDoStage); };
       bool ok = true;
       for (int it = 0; ok && it < total_it; ++it) {
         const bool graph = graph_of(it);
@@ -560,10 +573,10 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < QT / 16; ++kk)
-          mma_ts(tDK, tDP + ds_col(kk), make_sdesc(sQ + kk * 2048, L::kQChunk, 1024, kSwizzle128B),
+          mma_ts(tDK, tPT + 8 * kk, make_sdesc(sQ + kk * 2048, L::kQChunk, 1024, kSwizzle128B),
                  graph ? idesc_dkr : idesc_dk, (it > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&bars[kADkDone]);
-        mma_commit(&bars[kAQEmpty + (it & 1)]);
+        mma_commit(&bars[kAQEmpty + it % L::kQStages]);
         if (graph && (it % n_it) == n_it - 1 && it + 1 < total_it) mma_commit(&bars[kAHeadDone]);
       }
       if (ok) mma_commit(&bars[kAAllDone]);
@@ -590,13 +603,13 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
       const int h = hk * g + e;
       const bool graph = e < gh;
       for (int mi = 0; mi < n_it; ++mi, ++it) {
-        const int s = it & 1;
+        const int s = it % L::kQStages;
         const int m0 = (m_start + mi) * QT;
-        const float* lv = vec + s * 256;
+        const float* lv = vec + s * 2 * QT;
         // valid query columns q in [q_lo, q_hi) (tile-relative) for this key row
         const int q_hi = kv_valid ? min(QT, si.len_q - m0) : 0;
         const int q_lo = P.causal ? (kv_local - m0) : 0;
-        if (!mbar_wait(&bars[kAPrep + s], (it >> 1) & 1, abort_flag, 702) ||
+        if (!mbar_wait(&bars[kAPrep + s], (it / L::kQStages) & 1, abort_flag, 702) ||
             !mbar_wait(&bars[kASFull], it & 1, abort_flag, 701)) {
           ok = false;
           break;
@@ -614,8 +627,8 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
         uint32_t pk[QH / 2];
         p_chunk_bwd<32>(sv, pk, qw, q_lo, q_hi, lv, sl2);
         if constexpr (QH == 48) p_chunk_bwd<16>(sv + 32, pk + 16, qw + 32, q_lo, q_hi, lv, sl2);
-        // the P^T columns are free once the previous tile's dV has run
-        if (it > 0 && !mbar_wait(&bars[kADvDone], (it - 1) & 1, abort_flag, 703)) {
+        // the packed columns are free once the previous tile's dK has run
+        if (it > 0 && !mbar_wait(&bars[kADkDone], (it - 1) & 1, abort_flag, 703)) {
           ok = false;
           break;
         }
@@ -625,7 +638,8 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[kAPReady]);
-        // phase 2: dS^T = P^T (dP^T - Delta) into the first half of this warpgroup's dP^T columns
+        // phase 2: read dP^T (releasing it for the next tile), dS^T = P^T (dP^T - Delta)
+        // into the packed columns once dV has read P^T from them
         if (!mbar_wait(&bars[kADPFull], it & 1, abort_flag, 704)) {
           ok = false;
           break;
@@ -637,8 +651,16 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
           if constexpr (QH == 48) tmem_ld16(tDPw + 32, dp + 32);
           tmem_ld_wait32(dp);
           if constexpr (QH == 48) tmem_ld_wait16(dp + 32);
-          ds_chunk_bwd<QH>(pk, dp, dd, qw, lv);
-          tmem_st_packed<QH / 2>(tDPw, dd);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars[kADpRead]);
+          ds_chunk_bwd<QH>(pk, dp, dd, qw, lv + QT);
+          if (!mbar_wait(&bars[kADvDone], it & 1, abort_flag, 707)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          tmem_st_packed<QH / 2>(tPTw, dd);
         }
         tmem_st_wait();
         tc_fence_before();

@@ -7,6 +7,7 @@
 
 namespace fna2 {
 
+constexpr int kMaxDynamicSmem = 232448;  // 227 KB: dynamic shared memory per block on sm_100
 constexpr int kBlockM = 128;  // query rows per tile (one TMEM lane / softmax thread per row)
 constexpr int kBlockN = 128;  // key rows per tile
 constexpr float kLog2e = 1.4426950408889634f;
