@@ -5,24 +5,34 @@
 // (varlen): bias only on graph heads h < H_G, GQA kv_head = h / (H/H_KV),
 // causal on sequence-local positions, O = acc/(l+1e-6), LSE = m + log(l+1e-6).
 //
-// Design (one CTA per 128-row query tile of one head and sequence):
-//   warps 0-3  softmax: thread t owns query row t = TMEM lane t.  Reads the
-//              128x128 fp32 score tile S from TMEM, applies masks, keeps the
-//              running max/sum in registers, writes P (bf16) back into the
-//              same TMEM columns, rescales O in TMEM only when the max grew
-//              by more than 2^8 (exactly compensated at the end).
-//   warp 4     TMA producer: Q and R_q once; K(+R_k) and V tiles through two
-//              separate 2-stage mbarrier rings (K runs one tile ahead of V).
-//   warp 5     allocates 512 TMEM columns; one thread issues tcgen05.mma:
-//                S_b  = Q K^T + R~_q R_k^T   (SS, K = D + r_pad; the bias is an
-//                       extra K slice of the same accumulation, with
-//                       R~_q = R_q * gs/scale staged in shared memory)
-//                O   += P V                  (TS, P read from TMEM)
-// TMEM columns: O [0,128), S_0 [128,256), S_1 [256,384).
+// Design: one CTA per pair of 128-row query tiles (256 rows) of one head and
+// sequence, so that every K/V tile brought into shared memory feeds two score
+// tiles and two softmax warpgroups share each SM sub-partition's exp2 units.
+//   warps 0-3 / 4-7  softmax of query tile 0 / 1: thread t owns query row t
+//              of its tile = TMEM lane t.  Reads the 128x128 fp32 score tile
+//              from TMEM, applies masks, keeps the running max/sum in
+//              registers, writes P (bf16) back into the same TMEM columns,
+//              rescales O in TMEM only when the max grew by more than 2^8
+//              (exactly compensated at the end).
+//   warp 8     TMA producer: Q and R_q of both tiles once; K(+R_k) and V
+//              tiles through two separate 2-stage mbarrier rings.
+//   warp 9     allocates 512 TMEM columns; one thread issues tcgen05.mma:
+//                S_i  = Q_i K^T + R~_q,i R_k^T (SS, K = D + r_pad; the bias is
+//                       an extra K slice, R~_q = R_q * gs/scale in smem)
+//                O_i += P_i V                  (TS, P read from TMEM)
+//              in the order O_0 += P_0 V(j), S_0(j+1), O_1 += P_1 V(j),
+//              S_1(j+1): while one warpgroup turns S into P the tensor core
+//              works on the other tile.
+// TMEM columns: O_0 [0,128), O_1 [128,256), S_0 [256,384), S_1 [384,512).
+// S_i(j+1) overwrites P_i(j) only after O_i += P_i(j) V(j) (same issuing
+// thread, in order), and the commit that signals S_i(j+1) also covers
+// O_i += P_i(j) V(j), so a warpgroup that sees S_i(j+1) may rescale O_i.
 #include "fna2_kernels.cuh"
 #include "ptx.cuh"
 
 namespace fna2 {
+
+constexpr int kFwdTiles = 2;  // 128-row query tiles per CTA
 
 template <int D, int RP>
 struct FwdSmem {
@@ -33,61 +43,79 @@ struct FwdSmem {
   static constexpr int kVBytes = kBlockN * D * 2;
   static constexpr int kChunk = 128 * 128;  // one 64-column chunk of a 128-row tile (bytes)
   static constexpr int align(int x) { return (x + 1023) & ~1023; }
-  static constexpr int oQ = 0;
-  static constexpr int oRq = align(oQ + kQBytes);
-  static constexpr int oK0 = align(oRq + kRqBytes);
+  static constexpr int oQ = 0;                                    // Q_0, Q_1
+  static constexpr int oRq = align(oQ + kFwdTiles * kQBytes);     // R~_q,0, R~_q,1
+  static constexpr int oK0 = align(oRq + kFwdTiles * kRqBytes);
   static constexpr int oK1 = align(oK0 + kKBytes);
   static constexpr int oRk0 = align(oK1 + kKBytes);
   static constexpr int oRk1 = align(oRk0 + kRkBytes);
   static constexpr int oV0 = align(oRk1 + kRkBytes);
   static constexpr int oV1 = align(oV0 + kVBytes);
   static constexpr int oBar = align(oV1 + kVBytes);
-  static constexpr int kNumBars = 16;
+  static constexpr int kNumBars = 20;
   static constexpr int oMisc = oBar + kNumBars * 8;
-  static constexpr int kTotal = oMisc + 16 + 1024;  // + slack for runtime 1024 B alignment
+  static constexpr int kUsed = oMisc + 16;
+  // 1024 bytes of slack for aligning the base when they fit; otherwise the
+  // kernel checks that the dynamic shared memory base is 1024-byte aligned
+  static constexpr int kTotal = kUsed + 1024 <= kMaxDynamicSmem ? kUsed + 1024 : kUsed;
+  static_assert(kUsed <= kMaxDynamicSmem, "shared memory budget");
 };
 
 enum FwdBar {
   kBarQFull = 0,
-  kBarRqReady = 1,
-  kBarKFull = 2,    // +stage
-  kBarKEmpty = 4,   // +stage
-  kBarVFull = 6,    // +stage
-  kBarVEmpty = 8,   // +stage
-  kBarSFull = 10,   // +buffer
-  kBarPFull = 12,   // +buffer
-  kBarOReady = 14,
+  kBarRqReady = 1,   // +tile: R~_q,i scaled (one arrival per warp of warpgroup i)
+  kBarKFull = 3,     // +stage
+  kBarKEmpty = 5,    // +stage
+  kBarVFull = 7,     // +stage
+  kBarVEmpty = 9,    // +stage
+  kBarSFull = 11,    // +tile
+  kBarPFull = 13,    // +tile (one arrival per warp)
+  kBarAllDone = 15,
 };
 
+constexpr int kFwdThreads = 320;  // 2 softmax warpgroups, producer, MMA
+
 template <int D, int RP>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kFwdThreads, 1)
     fna2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmRq,
                     const __grid_constant__ CUtensorMap tmRk, const FwdParams p) {
   using L = FwdSmem<D, RP>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  if ((smem - smem_raw) + L::kUsed > L::kTotal) {  // layout does not fit the launch's shared memory
+    if (threadIdx.x == 0) atomicCAS(&g_device_error, 0, 199);
+    return;
+  }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::oBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::oMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::oMisc + 4);
 
   const ProblemDev& P = p.prob;
-  const int m_blk = p.n_mblocks - 1 - static_cast<int>(blockIdx.x);  // heaviest causal tiles first
+  const int n_pairs = (p.n_mblocks + 1) / 2;
+  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.x);  // heaviest causal tiles first
   const int h = blockIdx.y;
   const SeqInfo si = seq_info(P, blockIdx.z);
-  const int q0 = m_blk * kBlockM;
+  const int q0 = pair * 2 * kBlockM;
   if (q0 >= si.len_q) return;
   const int hk = h / (P.heads / P.heads_kv);
   const bool graph = h < P.heads_graph;
-  const int kv_end = P.causal ? min(si.len_k, q0 + kBlockM) : si.len_k;
-  const int n_tiles = kv_end > 0 ? (kv_end + kBlockN - 1) / kBlockN : 0;
+  // key tiles seen by each query tile (0 when the tile has no query row)
+  int n_t[kFwdTiles];
+#pragma unroll
+  for (int i = 0; i < kFwdTiles; ++i) {
+    const int qt = q0 + i * kBlockM;
+    const int kv_end = qt >= si.len_q ? 0 : (P.causal ? min(si.len_k, qt + kBlockM) : si.len_k);
+    n_t[i] = kv_end > 0 ? (kv_end + kBlockN - 1) / kBlockN : 0;
+  }
+  const int n_kv = max(n_t[0], n_t[1]);
   const int warp = warp_id();
   const int lane = lane_id();
   const int tid = threadIdx.x;
 
-  if (n_tiles == 0) {
+  if (n_kv == 0) {
     // No visible key: the reference's loop is empty, O = 0 and LSE = -inf.
-    if (tid < kBlockM && q0 + tid < si.len_q) {
+    if (tid < kFwdTiles * kBlockM && q0 + tid < si.len_q) {
       const int row = si.q_start + q0 + tid;
       __nv_bfloat16* orow = p.out + si.b * p.o_sb + h * p.o_sh + static_cast<int64_t>(row) * p.o_sr;
       for (int c = 0; c < D; ++c) orow[c] = __float2bfloat16(0.f);
@@ -98,20 +126,20 @@ __global__ void __launch_bounds__(192, 1)
 
   if (tid == 0) {
     mbar_init(&bars[kBarQFull], 1);
-    mbar_init(&bars[kBarRqReady], kBlockM);
     for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars[kBarRqReady + s], 4);
       mbar_init(&bars[kBarKFull + s], 1);
       mbar_init(&bars[kBarKEmpty + s], 1);
       mbar_init(&bars[kBarVFull + s], 1);
       mbar_init(&bars[kBarVEmpty + s], 1);
       mbar_init(&bars[kBarSFull + s], 1);
-      mbar_init(&bars[kBarPFull + s], kBlockM);
+      mbar_init(&bars[kBarPFull + s], 4);
     }
-    mbar_init(&bars[kBarOReady], 1);
+    mbar_init(&bars[kBarAllDone], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -120,7 +148,7 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
@@ -130,12 +158,20 @@ __global__ void __launch_bounds__(192, 1)
         tma_prefetch_desc(&tmRq);
         tma_prefetch_desc(&tmRk);
       }
-      const int qrow = si.q_start + q0;
-      mbar_expect_tx(&bars[kBarQFull], L::kQBytes + (graph ? L::kRqBytes : 0));
+      int q_bytes = 0;
 #pragma unroll
-      for (int c = 0; c < D / 64; ++c)
-        tma_load_4d(smem + L::oQ + c * L::kChunk, &tmQ, &bars[kBarQFull], c * 64, qrow, h, si.b);
-      if (graph) tma_load_4d(smem + L::oRq, &tmRq, &bars[kBarQFull], 0, qrow, h, si.b);
+      for (int i = 0; i < kFwdTiles; ++i)
+        if (n_t[i] > 0) q_bytes += L::kQBytes + (graph ? L::kRqBytes : 0);
+      mbar_expect_tx(&bars[kBarQFull], q_bytes);
+#pragma unroll
+      for (int i = 0; i < kFwdTiles; ++i) {
+        if (n_t[i] == 0) continue;
+        const int qrow = si.q_start + q0 + i * kBlockM;
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_4d(smem + L::oQ + i * L::kQBytes + c * L::kChunk, &tmQ, &bars[kBarQFull], c * 64, qrow, h, si.b);
+        if (graph) tma_load_4d(smem + L::oRq + i * L::kRqBytes, &tmRq, &bars[kBarQFull], 0, qrow, h, si.b);
+      }
 
       auto load_k = [&](int j) -> bool {
         const int s = j & 1;
@@ -161,32 +197,30 @@ __global__ void __launch_bounds__(192, 1)
         return true;
       };
       bool ok = load_k(0);
-      if (ok && n_tiles > 1) ok = load_k(1);
-      for (int j = 0; ok && j < n_tiles; ++j) {
+      if (ok && n_kv > 1) ok = load_k(1);
+      for (int j = 0; ok && j < n_kv; ++j) {
         ok = load_v(j);
-        if (ok && j + 2 < n_tiles) ok = load_k(j + 2);
+        if (ok && j + 2 < n_kv) ok = load_k(j + 2);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16(kBlockM, kBlockN, 0, 0);
       constexpr uint32_t idesc_pv = make_idesc_bf16(kBlockM, D, 0, 1);
       constexpr uint32_t r_layout = RP == 16 ? kSwizzle32B : (RP == 32 ? kSwizzle64B : kSwizzle128B);
       constexpr uint32_t r_sbo = 8 * RP * 2;
-      const uint32_t sQ = smem_u32(smem + L::oQ);
-      const uint32_t sRq = smem_u32(smem + L::oRq);
-      const uint32_t tO = tmem;
       bool ok = mbar_wait(&bars[kBarQFull], 0, abort_flag, 201);
-      if (ok && graph) ok = mbar_wait(&bars[kBarRqReady], 0, abort_flag, 202);
-      tc_fence_after();
+#pragma unroll
+      for (int i = 0; i < kFwdTiles; ++i)
+        if (ok && graph && n_t[i] > 0) ok = mbar_wait(&bars[kBarRqReady + i], 0, abort_flag, 202);
 
-      auto issue_s = [&](int j) -> bool {
+      // S_i(j) = Q_i K(j)^T (+ R~_q,i R_k(j)^T); the last user of K(j) releases its stage
+      auto issue_s = [&](int i, int j) {
         const int b = j & 1;
-        if (!mbar_wait(&bars[kBarKFull + b], (j >> 1) & 1, abort_flag, 203)) return false;
-        tc_fence_after();
+        const uint32_t sQ = smem_u32(smem + L::oQ + i * L::kQBytes);
         const uint32_t sK = smem_u32(smem + (b ? L::oK1 : L::oK0));
-        const uint32_t tS = tmem + 128 + 128 * b;
+        const uint32_t tS = tmem + 256 + 128 * i;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * L::kChunk + (kk & 3) * 32;
@@ -194,79 +228,101 @@ __global__ void __launch_bounds__(192, 1)
                  idesc_s, kk > 0);
         }
         if (graph) {
+          const uint32_t sRq = smem_u32(smem + L::oRq + i * L::kRqBytes);
           const uint32_t sRk = smem_u32(smem + (b ? L::oRk1 : L::oRk0));
 #pragma unroll
           for (int kk = 0; kk < RP / 16; ++kk)
             mma_ss(tS, make_sdesc(sRq + kk * 32, 16, r_sbo, r_layout), make_sdesc(sRk + kk * 32, 16, r_sbo, r_layout),
                    idesc_s, 1);
         }
-        mma_commit(&bars[kBarKEmpty + b]);
-        mma_commit(&bars[kBarSFull + b]);
+        mma_commit(&bars[kBarSFull + i]);
+        if (i == 1 || j >= n_t[1]) mma_commit(&bars[kBarKEmpty + b]);
+      };
+      auto wait_k = [&](int j) -> bool {
+        if (!mbar_wait_spin(&bars[kBarKFull + (j & 1)], (j >> 1) & 1, abort_flag, 203)) return false;
+        tc_fence_after();
         return true;
       };
 
-      if (ok) ok = issue_s(0);
-      if (ok && n_tiles > 1) ok = issue_s(1);
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        const int b = j & 1;
-        if (!mbar_wait(&bars[kBarPFull + b], (j >> 1) & 1, abort_flag, 204)) break;
-        if (!mbar_wait(&bars[kBarVFull + b], (j >> 1) & 1, abort_flag, 205)) break;
-        tc_fence_after();
-        const uint32_t sV = smem_u32(smem + (b ? L::oV1 : L::oV0));
-        const uint32_t tP = tmem + 128 + 128 * b;
+      if (ok) ok = wait_k(0);
+      if (ok) {
 #pragma unroll
-        for (int kk = 0; kk < kBlockN / 16; ++kk)
-          mma_ts(tO, tP + kk * 8, make_sdesc(sV + kk * 2048, L::kChunk, 1024, kSwizzle128B), idesc_pv,
-                 (j > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(&bars[kBarVEmpty + b]);
-        mma_commit(&bars[kBarOReady]);
-        if (j + 2 < n_tiles) ok = issue_s(j + 2);
+        for (int i = 0; i < kFwdTiles; ++i)
+          if (n_t[i] > 0) issue_s(i, 0);
       }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int b = j & 1;
+        const uint32_t sV = smem_u32(smem + (b ? L::oV1 : L::oV0));
+        if (!mbar_wait_spin(&bars[kBarVFull + b], (j >> 1) & 1, abort_flag, 205)) break;
+        if (j + 1 < n_kv && !wait_k(j + 1)) break;
+#pragma unroll
+        for (int i = 0; i < kFwdTiles; ++i) {
+          if (j >= n_t[i]) continue;
+          // O_i += P_i(j) V(j), then S_i(j+1) over the same TMEM columns
+          if (!mbar_wait_spin(&bars[kBarPFull + i], (j & 1), abort_flag, 204)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t tO = tmem + 128 * i;
+          const uint32_t tP = tmem + 256 + 128 * i;
+#pragma unroll
+          for (int kk = 0; kk < kBlockN / 16; ++kk)
+            mma_ts(tO, tP + kk * 8, make_sdesc(sV + kk * 2048, L::kChunk, 1024, kSwizzle128B), idesc_pv,
+                   (j > 0 || kk > 0) ? 1u : 0u);
+          if (j + 1 < n_t[i]) issue_s(i, j + 1);
+        }
+        mma_commit(&bars[kBarVEmpty + b]);
+      }
+      if (ok) mma_commit(&bars[kBarAllDone]);
     }
   } else {
-    // ------------------------------------------------------------ softmax (warps 0-3)
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t tO = tmem + lane_base;
-    const int q_local = q0 + tid;
+    // ------------------------------------------------------------ softmax (warpgroup i = query tile i)
+    const int wi = warp >> 2;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tO = tmem + 128 * wi + lane_base;
+    const uint32_t tSrow = tmem + 256 + 128 * wi + lane_base;
+    const int t = tid & 127;
+    const int q_local = q0 + wi * kBlockM + t;
+    const int n_my = n_t[wi];
     const float sl2 = P.scale_log2;
     bool ok = true;
 
-    if (graph) {
+    if (graph && n_my > 0) {
       // R~_q = R_q * gs/scale in place (element-wise, so independent of the swizzle).
       ok = mbar_wait(&bars[kBarQFull], 0, abort_flag, 301);
       if (ok) {
         const float f = __ldg(P.gs + h) / P.scale;
-        uint4* rrow = reinterpret_cast<uint4*>(smem + L::oRq + tid * RP * 2);
+        uint4* rrow = reinterpret_cast<uint4*>(smem + L::oRq + wi * L::kRqBytes + t * RP * 2);
 #pragma unroll
         for (int u = 0; u < RP / 8; ++u) {
           uint4 w = rrow[u];
           uint32_t* e = reinterpret_cast<uint32_t*>(&w);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            __nv_bfloat162 v2 = *reinterpret_cast<__nv_bfloat162*>(&e[i]);
+          for (int k = 0; k < 4; ++k) {
+            __nv_bfloat162 v2 = *reinterpret_cast<__nv_bfloat162*>(&e[k]);
             float2 f2 = __bfloat1622float2(v2);
-            e[i] = pack_bf16(f2.x * f, f2.y * f);
+            e[k] = pack_bf16(f2.x * f, f2.y * f);
           }
           rrow[u] = w;
         }
         fence_proxy_async_smem();
       }
-      mbar_arrive(&bars[kBarRqReady]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[kBarRqReady + wi]);
     }
 
     const int limit = P.causal ? min(si.len_k, q_local + 1) : si.len_k;
     float m_use = -INFINITY, m_true = -INFINITY, l = 0.f;
     uint32_t r[128];
-    for (int j = 0; ok && j < n_tiles; ++j) {
-      const int b = j & 1;
-      const uint32_t tS = tmem + lane_base + 128 + 128 * b;
-      if (!mbar_wait(&bars[kBarSFull + b], (j >> 1) & 1, abort_flag, 302)) {
+    for (int j = 0; ok && j < n_my; ++j) {
+      if (!mbar_wait(&bars[kBarSFull + wi], j & 1, abort_flag, 302)) {
         ok = false;
         break;
       }
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tS + 32 * c, r + 32 * c);
+      for (int c = 0; c < 4; ++c) tmem_ld32(tSrow + 32 * c, r + 32 * c);
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld_wait32(r + 32 * c);
 
@@ -274,12 +330,12 @@ __global__ void __launch_bounds__(192, 1)
       float mx = -INFINITY;
       if (nvalid >= kBlockN) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i) mx = fmaxf(mx, __uint_as_float(r[i]));
+        for (int k = 0; k < 128; ++k) mx = fmaxf(mx, __uint_as_float(r[k]));
       } else {
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
-          const float x = i < nvalid ? __uint_as_float(r[i]) : -INFINITY;
-          r[i] = __float_as_uint(x);
+        for (int k = 0; k < 128; ++k) {
+          const float x = k < nvalid ? __uint_as_float(r[k]) : -INFINITY;
+          r[k] = __float_as_uint(x);
           mx = fmaxf(mx, x);
         }
       }
@@ -296,44 +352,36 @@ __global__ void __launch_bounds__(192, 1)
       const float mb = (m_use == -INFINITY) ? 0.f : m_use;
       float rs = 0.f;
 #pragma unroll
-      for (int i = 0; i < 128; i += 2) {
-        const float p0 = ex2(fmaf(__uint_as_float(r[i]), sl2, -mb));
-        const float p1 = ex2(fmaf(__uint_as_float(r[i + 1]), sl2, -mb));
+      for (int k = 0; k < 128; k += 2) {
+        const float p0 = ex2(fmaf(__uint_as_float(r[k]), sl2, -mb));
+        const float p1 = ex2(fmaf(__uint_as_float(r[k + 1]), sl2, -mb));
         rs += p0 + p1;
-        r[i >> 1] = pack_bf16(p0, p1);
+        r[k >> 1] = pack_bf16(p0, p1);
       }
       l = l * alpha + rs;
       // P (bf16 pairs) over the first 64 columns of this S buffer
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_st16(tS + 16 * c, r + 16 * c);
-
-      if (j > 0) {
-        // previous P V must be complete before O is touched (and before the
-        // next S buffer can be reused by the issuer, which orders it anyway)
-        if (!mbar_wait(&bars[kBarOReady], (j - 1) & 1, abort_flag, 303)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, rescale)) {
-          const float a = rescale ? alpha : 1.f;
+      for (int c = 0; c < 4; ++c) tmem_st16(tSrow + 16 * c, r + 16 * c);
+      // O_i += P_i(j-1) V(j-1) is complete (covered by the S_i(j) commit): rescale O_i if needed
+      if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+        const float a = rescale ? alpha : 1.f;
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tO + 32 * c, o);
-            tmem_ld_wait32(o);
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + 32 * c, o);
+          tmem_ld_wait32(o);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * a);
-            tmem_st32(tO + 32 * c, o);
-          }
+          for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * a);
+          tmem_st32(tO + 32 * c, o);
         }
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&bars[kBarPFull + b]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[kBarPFull + wi]);
     }
 
-    if (ok && mbar_wait(&bars[kBarOReady], (n_tiles - 1) & 1, abort_flag, 304)) {
+    if (ok && n_my > 0 && mbar_wait(&bars[kBarAllDone], 0, abort_flag, 304)) {
       tc_fence_after();
       // exact reference normalisation with the true running max
       const float corr = (m_use == -INFINITY) ? 0.f : ex2(m_use - m_true);
@@ -351,11 +399,11 @@ __global__ void __launch_bounds__(192, 1)
           uint4 w[4];
           uint32_t* wp = reinterpret_cast<uint32_t*>(w);
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            wp[i] = pack_bf16(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+          for (int k = 0; k < 16; ++k)
+            wp[k] = pack_bf16(__uint_as_float(o[2 * k]) * inv, __uint_as_float(o[2 * k + 1]) * inv);
           uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = w[i];
+          for (int k = 0; k < 4; ++k) dst[k] = w[k];
         }
       }
       if (row_ok) {
@@ -367,7 +415,7 @@ __global__ void __launch_bounds__(192, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -383,8 +431,8 @@ cudaError_t launch_fwd_t(const CUtensorMap& q, const CUtensorMap& k, const CUten
   auto kern = fna2_fwd_kernel<D, RP>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
   if (e != cudaSuccess) return e;
-  dim3 grid(p.n_mblocks, grid_y, grid_z);
-  kern<<<grid, 192, L::kTotal, stream>>>(q, k, v, rq, rk, p);
+  dim3 grid((p.n_mblocks + 1) / 2, grid_y, grid_z);
+  kern<<<grid, kFwdThreads, L::kTotal, stream>>>(q, k, v, rq, rk, p);
   return cudaGetLastError();
 }
 
