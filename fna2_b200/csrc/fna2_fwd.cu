@@ -284,7 +284,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const uint32_t tSrow = tmem + 256 + 128 * wi + lane_base;
     const int t = tid & 127;
     const int q_local = q0 + wi * kBlockM + t;
-    const int n_my = n_t[wi];
+    const int n_my = wi ? n_t[1] : n_t[0];
     const float sl2 = P.scale_log2;
     bool ok = true;
 
@@ -327,18 +327,23 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       for (int c = 0; c < 4; ++c) tmem_ld_wait32(r + 32 * c);
 
       const int nvalid = limit - j * kBlockN;
-      float mx = -INFINITY;
+      // row max with 8 independent chains (a single chain of 128 dependent
+      // fmaxf would dominate the tile's latency)
+      float m8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m8[k] = -INFINITY;
       if (nvalid >= kBlockN) {
 #pragma unroll
-        for (int k = 0; k < 128; ++k) mx = fmaxf(mx, __uint_as_float(r[k]));
+        for (int k = 0; k < 128; ++k) m8[k & 7] = fmaxf(m8[k & 7], __uint_as_float(r[k]));
       } else {
 #pragma unroll
         for (int k = 0; k < 128; ++k) {
           const float x = k < nvalid ? __uint_as_float(r[k]) : -INFINITY;
           r[k] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
+          m8[k & 7] = fmaxf(m8[k & 7], x);
         }
       }
+      float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       mx *= sl2;
       m_true = fmaxf(m_true, mx);
       float alpha = 1.f;
@@ -350,15 +355,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         m_use = m_true;
       }
       const float mb = (m_use == -INFINITY) ? 0.f : m_use;
-      float rs = 0.f;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
 #pragma unroll
       for (int k = 0; k < 128; k += 2) {
         const float p0 = ex2(fmaf(__uint_as_float(r[k]), sl2, -mb));
         const float p1 = ex2(fmaf(__uint_as_float(r[k + 1]), sl2, -mb));
-        rs += p0 + p1;
+        rs4[(k >> 1) & 3] += p0 + p1;
         r[k >> 1] = pack_bf16(p0, p1);
       }
-      l = l * alpha + rs;
+      l = l * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
       // P (bf16 pairs) over the first 64 columns of this S buffer
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_st16(tSrow + 16 * c, r + 16 * c);
