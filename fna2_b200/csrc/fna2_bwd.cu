@@ -685,6 +685,7 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
     if (ok && mbar_wait(&bars[kAAllDone], 0, abort_flag, 706)) {
       tc_fence_after();
       // each warpgroup stores half of the D columns of dV and dK
+      // each warpgroup stores half of the D columns of dV and dK
       constexpr int kCols = D / 2;
       __nv_bfloat16* dvrow = p.dv + si.b * p.dv_sb + hk * p.dv_sh + krow * p.dv_sr + wg * kCols;
       __nv_bfloat16* dkrow = p.dk + si.b * p.dk_sb + hk * p.dk_sh + krow * p.dk_sr + wg * kCols;
@@ -1092,14 +1093,22 @@ __global__ void __launch_bounds__(kDqThreads, 1)
     }
     if (ok && mbar_wait(&bars[kBAllDone], 0, abort_flag, 1003)) {
       tc_fence_after();
+      // each warpgroup stores half of the D columns, through the (now idle) K ring
       constexpr int kCols = D / 2;
-      __nv_bfloat16* dqrow = p.dq + si.b * p.dq_sb + h * p.dq_sh + row * p.dq_sr + wg * kCols;
-#pragma unroll 1
-      for (int c = 0; c < kCols / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tDQ + lane_base + wg * kCols + 32 * c, v);
-        tmem_ld_wait32(v);
-        if (row_ok) store_row32(dqrow + 32 * c, v, scale);
+      {
+        uint32_t pk[kCols / 2];
+#pragma unroll
+        for (int c = 0; c < kCols / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tDQ + lane_base + wg * kCols + 32 * c, v);
+          tmem_ld_wait32(v);
+#pragma unroll
+          for (int k = 0; k < 16; ++k)
+            pk[16 * c + k] = pack_bf16(__uint_as_float(v[2 * k]) * scale, __uint_as_float(v[2 * k + 1]) * scale);
+        }
+        const int row0_local = q0 + (warp & 3) * 32;
+        __nv_bfloat16* dq0 = p.dq + si.b * p.dq_sb + h * p.dq_sh + (si.q_start + row0_local) * p.dq_sr + wg * kCols;
+        warp_store_rows<kCols / 2>(smem + L::oK + warp * 32 * kCols * 2, pk, dq0, p.dq_sr, si.len_q - row0_local);
       }
       if (graph && wg == 0) {
         // dR_q = gs * dS R_k (the extra accumulator columns); d_gs += sum_r R_q * dS R_k

@@ -325,4 +325,30 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
 __device__ __forceinline__ uint32_t warp_id() { return threadIdx.x >> 5; }
 
+// Store this warp's 32 rows (thread t holds row t's NU32 packed bf16 pairs) with
+// coalesced writes: each thread puts its row into a shared-memory staging buffer
+// (32 x 4*NU32 bytes, 16-byte granules XOR-swizzled by row), then each store
+// instruction writes whole row segments of 4*NU32 bytes.  Rows r >= nvalid are
+// not written.  row0 points at row 0's first element; rows are row_stride
+// elements apart.
+template <int NU32>
+__device__ __forceinline__ void warp_store_rows(uint8_t* stage, const uint32_t* v, __nv_bfloat16* row0,
+                                                int64_t row_stride, int nvalid) {
+  constexpr int G = NU32 / 4;        // 16-byte granules per row
+  constexpr int RPI = 32 / G;        // rows per store instruction
+  const int lane = lane_id();
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+    *reinterpret_cast<uint4*>(stage + lane * (16 * G) + ((g ^ (lane % G)) * 16)) =
+        make_uint4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < G; ++i) {
+    const int r = RPI * i + lane / G, g = lane % G;
+    const uint4 w = *reinterpret_cast<const uint4*>(stage + r * (16 * G) + ((g ^ (r % G)) * 16));
+    if (r < nvalid) *reinterpret_cast<uint4*>(row0 + r * row_stride + g * 8) = w;
+  }
+  __syncwarp();
+}
+
 }  // namespace fna2
