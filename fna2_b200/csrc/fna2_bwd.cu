@@ -685,19 +685,25 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
     if (ok && mbar_wait(&bars[kAAllDone], 0, abort_flag, 706)) {
       tc_fence_after();
       // each warpgroup stores half of the D columns of dV and dK
-      // each warpgroup stores half of the D columns of dV and dK
+      // each warpgroup stores half of the D columns of dV and dK, 32 columns at a
+      // time, coalesced through the (now idle) Q ring
       constexpr int kCols = D / 2;
-      __nv_bfloat16* dvrow = p.dv + si.b * p.dv_sb + hk * p.dv_sh + krow * p.dv_sr + wg * kCols;
-      __nv_bfloat16* dkrow = p.dk + si.b * p.dk_sb + hk * p.dk_sh + krow * p.dk_sr + wg * kCols;
+      const int row0_local = n0 + (warp & 3) * 32;
+      const int64_t row0 = si.k_start + row0_local;
+      uint8_t* stage = smem + L::oQ + warp * 32 * 64;
 #pragma unroll 1
-      for (int c = 0; c < kCols / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tDV + lane_base + wg * kCols + 32 * c, v);
+      for (int mc = 0; mc < 2 * (kCols / 32); ++mc) {  // (dV, dK) x 32-column chunks
+        const int m = mc / (kCols / 32), c = mc % (kCols / 32);
+        const float f = m == 0 ? 1.f : scale;
+        uint32_t v[32], pk[16];
+        tmem_ld32((m == 0 ? tDV : tDK) + lane_base + wg * kCols + 32 * c, v);
         tmem_ld_wait32(v);
-        if (kv_valid) store_row32(dvrow + 32 * c, v, 1.f);
-        tmem_ld32(tDK + lane_base + wg * kCols + 32 * c, v);
-        tmem_ld_wait32(v);
-        if (kv_valid) store_row32(dkrow + 32 * c, v, scale);
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+          pk[k] = pack_bf16(__uint_as_float(v[2 * k]) * f, __uint_as_float(v[2 * k + 1]) * f);
+        __nv_bfloat16* dst = m == 0 ? p.dv + si.b * p.dv_sb + hk * p.dv_sh + row0 * p.dv_sr + wg * kCols + 32 * c
+                                    : p.dk + si.b * p.dk_sb + hk * p.dk_sh + row0 * p.dk_sr + wg * kCols + 32 * c;
+        warp_store_rows<16>(stage, pk, dst, m == 0 ? p.dv_sr : p.dk_sr, si.len_k - row0_local);
       }
       if (wg == 0 && gh > 0 && gh == g) {
         // dR_k of the group's last head (a graph head; otherwise it was stored at its end)
