@@ -75,6 +75,23 @@ enum FwdBar {
 
 constexpr int kFwdThreads = 320;  // 2 softmax warpgroups, producer, MMA
 
+// Epilogue: this warp's 32 rows of O (TMEM, fp32) times inv, as bf16, 32
+// columns at a time through a 2 KB shared-memory staging buffer.  Kept out of
+// line so that the softmax loop's register allocation does not see it.
+template <int D>
+__device__ __noinline__ void store_o_rows(uint8_t* stage, uint32_t tO, float inv, __nv_bfloat16* o0,
+                                          int64_t row_stride, int nvalid) {
+#pragma unroll 1
+  for (int c = 0; c < D / 32; ++c) {
+    uint32_t o[32], pk[16];
+    tmem_ld32(tO + 32 * c, o);
+    tmem_ld_wait32(o);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) pk[k] = pack_bf16(__uint_as_float(o[2 * k]) * inv, __uint_as_float(o[2 * k + 1]) * inv);
+    warp_store_rows<16>(stage, pk, o0 + 32 * c, row_stride, nvalid);
+  }
+}
+
 template <int D, int RP>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     fna2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -394,23 +411,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const float inv = corr / (l_true + kEps);
       const bool row_ok = q_local < si.len_q;
       const int row = si.q_start + q_local;
-      __nv_bfloat16* orow = p.out + si.b * p.o_sb + h * p.o_sh + static_cast<int64_t>(row) * p.o_sr;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tO + 32 * c, o);
-        tmem_ld_wait32(o);
-        if (row_ok) {
-          uint4 w[4];
-          uint32_t* wp = reinterpret_cast<uint32_t*>(w);
-#pragma unroll
-          for (int k = 0; k < 16; ++k)
-            wp[k] = pack_bf16(__uint_as_float(o[2 * k]) * inv, __uint_as_float(o[2 * k + 1]) * inv);
-          uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) dst[k] = w[k];
-        }
-      }
+      // O rows, 32 columns at a time, coalesced through the (now idle) K ring
+      const int row0_local = q0 + wi * kBlockM + (warp & 3) * 32;
+      __nv_bfloat16* o0 = p.out + si.b * p.o_sb + h * p.o_sh + static_cast<int64_t>(si.q_start + row0_local) * p.o_sr;
+      store_o_rows<D>(smem + L::oK0 + warp * 32 * 64, tO, inv, o0, p.o_sr, si.len_q - row0_local);
       if (row_ok) {
         const float lse = (m_true == -INFINITY) ? -INFINITY : (m_true + lg2(l_true + kEps)) * kLn2;
         p.lse[(static_cast<int64_t>(si.b) * P.heads + h) * p.lse_sbh + row] = lse;
