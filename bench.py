@@ -16,6 +16,11 @@ pinned host memory and d_graph_scale read back every step.
 ``--impl reference`` times the reference's eager path restated on the CPU
 (oracle/fna2_oracle.py: materialised bias + SDPA + autograd, fp32, all host
 threads) on a bounded sample of the same workload.
+
+``--op qk_prep`` instead measures the fused varlen QK-RMSNorm + RoPE transform
+(fna2_b200/qk_prep.py) forward + backward on the workload's q and k (bf16,
+H_KV = H), as HBM GB/s against the measured copy bandwidth, with the
+reference's per-sequence CPU path (oracle/qk_prep_oracle.py) timed beside it.
 """
 from __future__ import annotations
 
@@ -357,6 +362,82 @@ def run_gpu(args, w):
         dist.destroy_process_group()
 
 
+def run_qk_prep(args, w):
+    """Fused varlen QK-RMSNorm + RoPE, forward + backward, one GPU."""
+    import types
+    from fna2_b200.qk_prep import apply_qk_norm_rope_varlen
+    from oracle import qk_prep_oracle as QO
+    dev = "cuda"
+    lengths, H, D = w["lengths"], w["H"], w["D"]
+    T = sum(lengths)
+    cu = torch.tensor([0] + list(torch.tensor(lengths).cumsum(0).tolist()), dtype=torch.int32, device=dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(T, H, D, device=dev, generator=g).bfloat16().requires_grad_(True)
+    k = torch.randn(T, H, D, device=dev, generator=g).bfloat16().requires_grad_(True)
+    norms = [types.SimpleNamespace(weight=torch.ones(D, device=dev, dtype=torch.bfloat16).requires_grad_(True),
+                                   eps=1e-6) for _ in range(2)]
+    rope = types.SimpleNamespace(inv_freq=QO.rope_inv_freq(D))
+    gq = torch.randn(T, H, D, device=dev, generator=g).bfloat16()
+    gk = torch.randn(T, H, D, device=dev, generator=g).bfloat16()
+
+    def step():
+        qo, ko = apply_qk_norm_rope_varlen(q, k, cu, norms[0], norms[1], rope)
+        torch.autograd.backward([qo, ko], [gq, gk])
+
+    for _ in range(args.warmup):
+        step()
+    st = torch.cuda.current_stream()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(0)
+    torch.cuda.synchronize()
+    clocks.start()
+    t0.record(st)
+    for _ in range(args.steps):
+        step()
+    t1.record(st)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    rows = T * 2 * H * D  # elements of q and k together
+    # forward reads x (bf16) and writes y (bf16); backward reads x and dy, writes dx (all bf16)
+    algo_bytes = rows * (2 + 2) + rows * (2 + 2 + 2)
+    gbs = algo_bytes / (ms / 1e3) / 1e9
+    peak = None
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = json.load(f).get("hbm_gbs")
+    except Exception:
+        pass
+    peak_src = "measured"
+    if peak is None:
+        peak, peak_src = 6650.0, "fallback"
+    # CPU: the reference path restated (norm + per-sequence RoPE loop + autograd), fp32, sample of sequences
+    cpu = None
+    if not args.no_cpu:
+        torch.set_num_threads(os.cpu_count())
+        sample = []
+        for L in lengths:  # whole short sequences of the workload, about 16k tokens
+            if L <= 1024 and sum(sample) + L <= 16384:
+                sample.append(L)
+        qc, kc, wq, wk, inv, cuc, dqo, dko = QO.make_inputs(sample, H, H, D, 0)
+        t_c = time.perf_counter()
+        QO.qk_prep_with_grads(qc, kc, cuc, wq, wk, 1e-6, inv, dqo, dko)
+        dt = time.perf_counter() - t_c
+        cb = sum(sample) * 2 * H * D * (4 + 2 + 4 + 2 + 4)
+        cpu = {"value": cb / dt / 1e9, "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"{len(sample)} sequences of the workload with L<=1024 (sum L={sum(sample)}), fp32, "
+                         f"{dt:.2f} s"}
+    print(json.dumps({
+        "metric": "qk_prep fwd+bwd GB/s (varlen QK-RMSNorm + RoPE, bf16)", "value": gbs, "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": w["desc"] + "; q and k of every token, H_KV = H", "tokens": T},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                     "peak_source": peak_src, "algorithmic_bytes_per_step": algo_bytes},
+        "cpu_baseline": cpu, "clocks": clk,
+    }))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -367,9 +448,12 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--op", default="attention", choices=["attention", "qk_prep"])
     args = ap.parse_args()
     w = workload(args.workload)
-    if args.impl == "reference":
+    if args.op == "qk_prep":
+        run_qk_prep(args, w)
+    elif args.impl == "reference":
         run_reference(args, w)
     else:
         run_gpu(args, w)

@@ -12,14 +12,16 @@ from typing import Optional
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("FNA2_LIB", os.path.join(HERE, "libfna2_b200.so"))
 
-FNA2_ABI_VERSION = 1
+FNA2_ABI_VERSION = 2
 FNA2_OK = 0
 FNA2_ERR_INVALID = -1
 FNA2_ERR_CUDA = -2
 FNA2_ERR_WORKSPACE = -3
 
 EXPORTED = ["fna2_fwd", "fna2_bwd", "fna2_bwd_workspace_size", "fna2_last_error", "fna2_device_status",
-            "fna2_abi_version", "fna2_bwd_noalloc"]
+            "fna2_abi_version", "fna2_bwd_noalloc", "fna2_qk_prep_fwd", "fna2_qk_prep_bwd"]
+FNA2_DTYPE_F32 = 0
+FNA2_DTYPE_BF16 = 1
 NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024  # FNA2_NOALLOC_SCRATCH_BYTES
 
 
@@ -85,6 +87,44 @@ class Fna2BwdArgs(ctypes.Structure):
     ]
 
 
+class Fna2Rows(ctypes.Structure):
+    _fields_ = [("ptr", ctypes.c_void_p), ("token_stride", ctypes.c_int64), ("head_stride", ctypes.c_int64)]
+
+
+class Fna2QkPrepArgs(ctypes.Structure):
+    _fields_ = [
+        ("total_tokens", ctypes.c_int64),
+        ("num_seqs", ctypes.c_int32),
+        ("cu_seqlens", ctypes.c_void_p),
+        ("heads_q", ctypes.c_int32),
+        ("heads_k", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("in_dtype", ctypes.c_int32),
+        ("weight_dtype", ctypes.c_int32),
+        ("rope_dtype", ctypes.c_int32),
+        ("q_in", Fna2Rows),
+        ("k_in", Fna2Rows),
+        ("q_out", Fna2Rows),
+        ("k_out", Fna2Rows),
+        ("q_weight", ctypes.c_void_p),
+        ("k_weight", ctypes.c_void_p),
+        ("eps", ctypes.c_float),
+        ("inv_freq", ctypes.c_void_p),
+    ]
+
+
+class Fna2QkPrepBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("fwd", Fna2QkPrepArgs),
+        ("dq_out", Fna2Rows),
+        ("dk_out", Fna2Rows),
+        ("dq_in", Fna2Rows),
+        ("dk_in", Fna2Rows),
+        ("dq_weight", ctypes.c_void_p),
+        ("dk_weight", ctypes.c_void_p),
+    ]
+
+
 _lib: Optional[ctypes.CDLL] = None
 
 
@@ -104,6 +144,10 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.fna2_bwd.restype = ctypes.c_int
     lib.fna2_bwd_noalloc.argtypes = [ctypes.POINTER(Fna2BwdArgs), ctypes.c_void_p]
     lib.fna2_bwd_noalloc.restype = ctypes.c_int
+    lib.fna2_qk_prep_fwd.argtypes = [ctypes.POINTER(Fna2QkPrepArgs), ctypes.c_void_p]
+    lib.fna2_qk_prep_fwd.restype = ctypes.c_int
+    lib.fna2_qk_prep_bwd.argtypes = [ctypes.POINTER(Fna2QkPrepBwdArgs), ctypes.c_void_p]
+    lib.fna2_qk_prep_bwd.restype = ctypes.c_int
     lib.fna2_bwd_workspace_size.argtypes = [ctypes.POINTER(Fna2Problem)]
     lib.fna2_bwd_workspace_size.restype = ctypes.c_size_t
     lib.fna2_last_error.argtypes = []

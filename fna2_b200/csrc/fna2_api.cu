@@ -16,6 +16,7 @@
 
 #include "fna2_bwd.cu"
 #include "fna2_fwd.cu"
+#include "fna2_qkprep.cu"
 
 namespace fna2 {
 namespace {
@@ -346,3 +347,90 @@ extern "C" int fna2_bwd(const Fna2BwdArgs* a, void* stream) {
 
 // The no-allocation backward entry point (fna2_bwd_noalloc) and its static scratch.
 #include "fna2_noalloc.cu"
+
+// ---------------------------------------------------------------------------
+// varlen QK-RMSNorm + RoPE
+// ---------------------------------------------------------------------------
+namespace fna2 {
+namespace {
+
+int check_rows(const Fna2Rows& r, int heads, int elem_bytes, int D, const char* what) {
+  if (heads == 0) return FNA2_OK;
+  FNA2_CHECK(r.ptr != nullptr, "%s: null pointer", what);
+  FNA2_CHECK(reinterpret_cast<uintptr_t>(r.ptr) % 16 == 0, "%s: base pointer must be 16-byte aligned", what);
+  const int64_t vec = 16 / elem_bytes;
+  FNA2_CHECK(r.token_stride % vec == 0 && r.head_stride % vec == 0,
+             "%s: token/head strides must be multiples of %lld elements", what, static_cast<long long>(vec));
+  FNA2_CHECK(r.token_stride >= 0 && r.head_stride >= 0, "%s: negative stride", what);
+  (void)D;
+  return FNA2_OK;
+}
+
+int qk_prep_params(const Fna2QkPrepArgs* a, QkPrepParams* p) {
+  FNA2_CHECK(a != nullptr, "null arguments");
+  FNA2_CHECK(a->head_dim == 64 || a->head_dim == 128, "head_dim must be 64 or 128 (got %d)", a->head_dim);
+  FNA2_CHECK(a->total_tokens >= 0 && a->heads_q >= 0 && a->heads_k >= 0, "negative size");
+  FNA2_CHECK(a->in_dtype == FNA2_DTYPE_F32 || a->in_dtype == FNA2_DTYPE_BF16, "bad in_dtype %d", a->in_dtype);
+  FNA2_CHECK(a->weight_dtype == FNA2_DTYPE_F32 || a->weight_dtype == FNA2_DTYPE_BF16, "bad weight_dtype %d",
+             a->weight_dtype);
+  FNA2_CHECK(a->rope_dtype == FNA2_DTYPE_F32 || a->rope_dtype == FNA2_DTYPE_BF16, "bad rope_dtype %d", a->rope_dtype);
+  FNA2_CHECK((a->q_weight == nullptr) == (a->k_weight == nullptr), "set both RMSNorm weights or neither");
+  FNA2_CHECK(a->eps >= 0.f, "eps must be >= 0");
+  if (a->inv_freq) FNA2_CHECK(a->cu_seqlens != nullptr && a->num_seqs >= 1, "RoPE needs cu_seqlens with >= 1 sequence");
+  const int in_bytes = a->in_dtype == FNA2_DTYPE_BF16 ? 2 : 4;
+  if (int rc = check_rows(a->q_in, a->heads_q, in_bytes, a->head_dim, "q_in")) return rc;
+  if (int rc = check_rows(a->k_in, a->heads_k, in_bytes, a->head_dim, "k_in")) return rc;
+  std::memset(p, 0, sizeof(*p));
+  p->T = a->total_tokens;
+  p->N = a->num_seqs;
+  p->cu = a->cu_seqlens;
+  p->hq = a->heads_q;
+  p->hk = a->heads_k;
+  p->in_bf16 = a->in_dtype == FNA2_DTYPE_BF16;
+  p->w_bf16 = a->weight_dtype == FNA2_DTYPE_BF16;
+  p->rope_bf16 = a->rope_dtype == FNA2_DTYPE_BF16;
+  p->qi = {const_cast<void*>(a->q_in.ptr), a->q_in.token_stride, a->q_in.head_stride};
+  p->ki = {const_cast<void*>(a->k_in.ptr), a->k_in.token_stride, a->k_in.head_stride};
+  p->qw = a->q_weight;
+  p->kw = a->k_weight;
+  p->eps = a->eps;
+  p->inv_freq = a->inv_freq;
+  return FNA2_OK;
+}
+
+}  // namespace
+}  // namespace fna2
+
+extern "C" int fna2_qk_prep_fwd(const Fna2QkPrepArgs* a, void* stream) {
+  QkPrepParams p;
+  if (int rc = qk_prep_params(a, &p)) return rc;
+  if (int rc = check_rows(a->q_out, a->heads_q, 2, a->head_dim, "q_out")) return rc;
+  if (int rc = check_rows(a->k_out, a->heads_k, 2, a->head_dim, "k_out")) return rc;
+  p.qo = {a->q_out.ptr, a->q_out.token_stride, a->q_out.head_stride};
+  p.ko = {a->k_out.ptr, a->k_out.token_stride, a->k_out.head_stride};
+  if (p.T == 0 || p.hq + p.hk == 0) return FNA2_OK;
+  FNA2_CUDA(launch_qk_prep(p, a->head_dim, false, static_cast<cudaStream_t>(stream)));
+  return FNA2_OK;
+}
+
+extern "C" int fna2_qk_prep_bwd(const Fna2QkPrepBwdArgs* b, void* stream) {
+  FNA2_CHECK(b != nullptr, "null arguments");
+  const Fna2QkPrepArgs* a = &b->fwd;
+  QkPrepParams p;
+  if (int rc = qk_prep_params(a, &p)) return rc;
+  const int in_bytes = a->in_dtype == FNA2_DTYPE_BF16 ? 2 : 4;
+  if (int rc = check_rows(b->dq_out, a->heads_q, 2, a->head_dim, "dq_out")) return rc;
+  if (int rc = check_rows(b->dk_out, a->heads_k, 2, a->head_dim, "dk_out")) return rc;
+  if (int rc = check_rows(b->dq_in, a->heads_q, in_bytes, a->head_dim, "dq_in")) return rc;
+  if (int rc = check_rows(b->dk_in, a->heads_k, in_bytes, a->head_dim, "dk_in")) return rc;
+  if (a->q_weight) FNA2_CHECK(b->dq_weight != nullptr && b->dk_weight != nullptr, "weight gradients needed");
+  p.dqo = {const_cast<void*>(b->dq_out.ptr), b->dq_out.token_stride, b->dq_out.head_stride};
+  p.dko = {const_cast<void*>(b->dk_out.ptr), b->dk_out.token_stride, b->dk_out.head_stride};
+  p.dqi = {b->dq_in.ptr, b->dq_in.token_stride, b->dq_in.head_stride};
+  p.dki = {b->dk_in.ptr, b->dk_in.token_stride, b->dk_in.head_stride};
+  p.dqw = a->q_weight ? b->dq_weight : nullptr;
+  p.dkw = a->q_weight ? b->dk_weight : nullptr;
+  if (p.T == 0 || p.hq + p.hk == 0) return FNA2_OK;
+  FNA2_CUDA(launch_qk_prep(p, a->head_dim, true, static_cast<cudaStream_t>(stream)));
+  return FNA2_OK;
+}

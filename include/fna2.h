@@ -50,7 +50,7 @@
 extern "C" {
 #endif
 
-#define FNA2_ABI_VERSION 1
+#define FNA2_ABI_VERSION 2
 
 #define FNA2_OK 0
 #define FNA2_ERR_INVALID (-1)
@@ -128,6 +128,63 @@ int fna2_bwd(const Fna2BwdArgs* args, void* stream);
  * overlaps race on it, so order them on one stream.  Calls no cudaMalloc or
  * cudaFree. */
 int fna2_bwd_noalloc(const Fna2BwdArgs* args, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Varlen QK-RMSNorm + RoPE: the transform NaylisAttention._forward_varlen
+ * applies to q and k before the attention (FNA2/attention_fna2.py:558-566:
+ * RMSNorm :94-102, RotaryPositionalEmbedding :108-163, _apply_rope_varlen
+ * :620-647), fused into one pass whose positions restart at 0 for every
+ * packed sequence (the reference loops over sequences on the host after a
+ * .tolist() sync).  Per row x (one token, one head, head_dim values):
+ *   n = x * rsqrt(mean(x^2) + eps) * w                 (if the weight is set)
+ *   y = n * cos(pos * f) + rotate_half(n) * sin(pos * f) (if inv_freq is set)
+ * with f = inv_freq repeated twice over head_dim, pos the token's index
+ * within its sequence, rotate_half(n) = [-n[D/2:], n[:D/2]], and y stored
+ * as bf16 (the attention's input dtype).  The cos/sin table is formed in
+ * rope_dtype as the reference does (in bf16, positions and angles are
+ * rounded to bf16 first).  Tokens outside [cu[0], cu[N]) are not written by
+ * the forward when RoPE is on (the reference leaves them unset) and get zero
+ * gradients.  head_dim is 64 or 128.
+ * Replace: RMSNorm.forward (attention_fna2.py:100-102) on q and k, and
+ * NaylisAttention._apply_rope_varlen (:620-647). */
+#define FNA2_DTYPE_F32 0
+#define FNA2_DTYPE_BF16 1
+
+typedef struct Fna2Rows { /* [T, heads, head_dim] rows, column stride 1 */
+  void* ptr;
+  int64_t token_stride; /* elements */
+  int64_t head_stride;  /* elements */
+} Fna2Rows;
+
+typedef struct Fna2QkPrepArgs {
+  int64_t total_tokens;       /* T */
+  int num_seqs;               /* N */
+  const int32_t* cu_seqlens;  /* [N+1], device */
+  int heads_q, heads_k, head_dim;
+  int in_dtype;               /* dtype of q_in and k_in (FNA2_DTYPE_*) */
+  int weight_dtype;           /* dtype of q_weight and k_weight */
+  int rope_dtype;             /* dtype of the tensor entering RoPE in the reference */
+  Fna2Rows q_in, k_in;
+  Fna2Rows q_out, k_out;      /* bf16 */
+  const void* q_weight;       /* [head_dim] RMSNorm weight, or NULL: no norm */
+  const void* k_weight;
+  float eps;
+  const float* inv_freq;      /* [head_dim/2] fp32, or NULL: no RoPE */
+} Fna2QkPrepArgs;
+
+/* Forward of the transform above. */
+int fna2_qk_prep_fwd(const Fna2QkPrepArgs* args, void* stream);
+
+typedef struct Fna2QkPrepBwdArgs {
+  Fna2QkPrepArgs fwd;         /* the forward's arguments; q_in/k_in are read again, q_out/k_out unused */
+  Fna2Rows dq_out, dk_out;    /* gradients of the bf16 outputs (bf16) */
+  Fna2Rows dq_in, dk_in;      /* written, in in_dtype */
+  float* dq_weight;           /* [head_dim] fp32, accumulated into (zero it first), or NULL */
+  float* dk_weight;
+} Fna2QkPrepBwdArgs;
+
+/* Backward of the transform: gradients of q_in, k_in and of the two weights. */
+int fna2_qk_prep_bwd(const Fna2QkPrepBwdArgs* args, void* stream);
 
 /* Message of the last failed call on this host thread ("" if none). */
 const char* fna2_last_error(void);

@@ -46,6 +46,65 @@ def test_struct_layout_matches_c(tmp_path):
     assert got == want
 
 
+def test_qkprep_struct_layout_matches_c(tmp_path):
+    src = tmp_path / "sz2.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "fna2.h"\n'
+                   'int main(){printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(Fna2Rows), sizeof(Fna2QkPrepArgs),'
+                   ' sizeof(Fna2QkPrepBwdArgs), offsetof(Fna2QkPrepArgs, inv_freq), offsetof(Fna2QkPrepArgs, q_in),'
+                   ' offsetof(Fna2QkPrepBwdArgs, dk_weight));}\n')
+    exe = tmp_path / "sz2"
+    subprocess.check_call(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)])
+    got = [int(x) for x in subprocess.check_output([str(exe)]).split()]
+    want = [ctypes.sizeof(_lib.Fna2Rows), ctypes.sizeof(_lib.Fna2QkPrepArgs), ctypes.sizeof(_lib.Fna2QkPrepBwdArgs),
+            _lib.Fna2QkPrepArgs.inv_freq.offset, _lib.Fna2QkPrepArgs.q_in.offset,
+            _lib.Fna2QkPrepBwdArgs.dk_weight.offset]
+    assert got == want
+
+
+def _qk_args(**over):
+    a = _lib.Fna2QkPrepArgs()
+    a.total_tokens, a.num_seqs, a.heads_q, a.heads_k, a.head_dim = 8, 1, 2, 1, 128
+    a.in_dtype = a.weight_dtype = a.rope_dtype = _lib.FNA2_DTYPE_BF16
+    buf = ctypes.create_string_buffer(1 << 16)
+    base = (ctypes.addressof(buf) + 255) // 256 * 256
+    for name in ("q_in", "k_in", "q_out", "k_out"):
+        setattr(a, name, _lib.Fna2Rows(base, 256, 128))
+    for k, v in over.items():
+        setattr(a, k, v)
+    return a, buf
+
+
+@pytest.mark.parametrize("field,value,msg", [
+    ("head_dim", 96, "head_dim"),
+    ("in_dtype", 7, "in_dtype"),
+    ("rope_dtype", -1, "rope_dtype"),
+    ("total_tokens", -1, "negative"),
+])
+def test_qkprep_invalid_arguments_rejected(field, value, msg):
+    lib = _lib.load()
+    a, _buf = _qk_args(**{field: value})
+    assert lib.fna2_qk_prep_fwd(a, None) == _lib.FNA2_ERR_INVALID
+    assert msg in lib.fna2_last_error().decode()
+
+
+def test_qkprep_rope_needs_cu_and_alignment():
+    lib = _lib.load()
+    inv = (ctypes.c_float * 64)()
+    a, _buf = _qk_args(inv_freq=ctypes.addressof(inv))
+    assert lib.fna2_qk_prep_fwd(a, None) == _lib.FNA2_ERR_INVALID
+    assert "cu_seqlens" in lib.fna2_last_error().decode()
+    a, _buf = _qk_args()
+    a.q_in = _lib.Fna2Rows(a.q_in.ptr + 2, 256, 128)
+    assert lib.fna2_qk_prep_fwd(a, None) == _lib.FNA2_ERR_INVALID
+    assert "aligned" in lib.fna2_last_error().decode()
+
+
+def test_qkprep_empty_is_a_no_op():
+    lib = _lib.load()
+    a, _buf = _qk_args(total_tokens=0)
+    assert lib.fna2_qk_prep_fwd(a, None) == _lib.FNA2_OK
+
+
 def _fwd_args(**over):
     a = _lib.Fna2FwdArgs()
     p = a.prob
