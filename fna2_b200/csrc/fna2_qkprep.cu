@@ -8,13 +8,11 @@
 //
 // HBM-bound elementwise work.  Each warp owns a contiguous run of tokens and
 // streams the rows (token, head) of that run through a small ring of
-// asynchronous copies in shared memory; a row is spread over head_dim/16 lanes
-// so that both halves of every rotate_half pair sit in one lane.  A token's
-// position comes from a warp-wide search over cu_seqlens (skipped while the
-// run stays inside one sequence) and its cos/sin values are computed once and
-// reused for all of its heads.  The backward recomputes the norm and reduces
-// the weight gradients per warp, then per CTA, then with one atomic per
-// column and CTA.
+// asynchronous copies in shared memory.  A token's position comes from a
+// warp-wide search over cu_seqlens (skipped while the run stays inside one
+// sequence) and its cos/sin values are computed once and reused for all of its
+// heads.  The backward recomputes the norm and reduces the weight gradients
+// per warp, then per CTA, then with one atomic per column and CTA.
 #include "fna2_kernels.cuh"
 
 namespace fna2 {
@@ -41,20 +39,31 @@ struct QkPrepParams {
 };
 
 constexpr int kPrepThreads = 256;
-constexpr int kRowBatch = 2;     // row instructions per streamed unit (forward)
-constexpr int kRowBatchBwd = 1;  // the same for the backward (twice the operands per row)
+
+// Field-wise select of one of two row descriptors.  Selecting a reference to a
+// kernel parameter at run time would make the compiler copy the parameters to
+// local memory.
+__device__ __forceinline__ QkRows pick(bool first, const QkRows& a, const QkRows& b) {
+  QkRows r;
+  r.ptr = first ? a.ptr : b.ptr;
+  r.ts = first ? a.ts : b.ts;
+  r.hs = first ? a.hs : b.hs;
+  return r;
+}
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
-// Layout: a row (one token, one head, D values) is spread over LPR = D/16 lanes;
-// lane `sub` of a row holds the 8 values [8*sub, 8*sub+8) of the first half and
-// the 8 values [D/2 + 8*sub, ...) of the second half, so the rotate_half pairs
-// (e, e + D/2) sit in the same lane and RoPE needs no shuffles; row sums reduce
-// over the row's LPR lanes.  A warp covers RPW = 32/LPR rows per instruction.
-// Inputs stream through a per-warp ring of asynchronous copies (kPrepStages row
-// batches deep); each lane reads back only the 16-byte pieces it copied.
+// Layout.  Rows move between HBM and shared memory as whole rows: piece i
+// (16 bytes) of a unit of RB rows is copied by lane i % 32, so each warp
+// instruction covers whole rows (instructions that cover half rows, 128 bytes
+// apart, measured at two thirds of the bandwidth).  For the arithmetic a row
+// is spread over LPR = D/16 lanes: lane `sub` of a row holds the 8 values
+// [8*sub, 8*sub+8) of the first half and the 8 values [D/2 + 8*sub, ...) of
+// the second half, so the rotate_half pairs (e, e + D/2) sit in one lane and
+// RoPE needs no shuffles; row sums reduce over the row's LPR lanes.  A warp
+// covers RPW = 32/LPR rows per row batch.
 constexpr int kHPL = 8;         // values per lane per half row
-constexpr int kPrepStages = 4;  // row batches in flight per warp
+constexpr int kPrepStages = 4;  // units in flight per warp
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(valid ? 16 : 0)
@@ -64,52 +73,70 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// Copy this lane's two half-row pieces (8 values each) of one row into dst.
-__device__ __forceinline__ void stage_row(uint8_t* dst, const void* base, int64_t row_off, int D, int sub,
-                                          int in_bytes, bool valid) {
-  const uint8_t* b = static_cast<const uint8_t*>(base);
+// Address of global row rr (< hq: a query head of A, else a key head of B) of token t.
+template <int ES>
+__device__ __forceinline__ uint8_t* row_addr(const QkPrepParams& p, const QkRows& A, const QkRows& B, int64_t t,
+                                             int rr) {
+  const bool isq = rr < p.hq;
+  const QkRows m = pick(isq, A, B);
+  return static_cast<uint8_t*>(m.ptr) + (t * m.ts + static_cast<int64_t>(isq ? rr : rr - p.hq) * m.hs) * ES;
+}
+
+// Copy global rows [row0, row0 + RB) of token t into a row-major block at dst
+// (rows past hq + hk are zero-filled).
+template <int D, int RB, int ES>
+__device__ __forceinline__ void stage_rows(uint8_t* dst, const QkPrepParams& p, const QkRows& A, const QkRows& B,
+                                           int64_t t, int row0, int lane) {
+  constexpr int PPR = D * ES / 16;  // 16-byte pieces per row
+  static_assert((RB * PPR) % 32 == 0, "a unit is whole warp instructions");
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const uint8_t* src = b + (row_off + h * (D / 2) + kHPL * sub) * in_bytes;
-    uint8_t* d = dst + h * kHPL * in_bytes;
-    cp_async16(d, valid ? src : b, valid);
-    if (in_bytes == 4) cp_async16(d + 16, valid ? src + 16 : b, valid);
+  for (int i = 0; i < RB * PPR / 32; ++i) {
+    const int q = i * 32 + lane, rr = row0 + q / PPR;
+    const bool valid = rr < p.hq + p.hk;
+    const uint8_t* g = valid ? row_addr<ES>(p, A, B, t, rr) + (q % PPR) * 16 : static_cast<const uint8_t*>(A.ptr);
+    cp_async16(dst + q * 16, g, valid);
   }
 }
 
-// Read back the staged pieces as x1 (first half) and x2 (second half).
-__device__ __forceinline__ void unstage_row(const uint8_t* src, bool is_bf16, float (&x1)[kHPL], float (&x2)[kHPL]) {
+// Store the row-major block at src as global rows [row0, row0 + RB) of token t.
+template <int D, int RB, int ES>
+__device__ __forceinline__ void store_rows(const uint8_t* src, const QkPrepParams& p, const QkRows& A,
+                                           const QkRows& B, int64_t t, int row0, int lane) {
+  constexpr int PPR = D * ES / 16;
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    float* x = h ? x2 : x1;
-    if (is_bf16) {
-      const uint4 w = *reinterpret_cast<const uint4*>(src + h * kHPL * 2);
-      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+  for (int i = 0; i < RB * PPR / 32; ++i) {
+    const int q = i * 32 + lane, rr = row0 + q / PPR;
+    if (rr < p.hq + p.hk)
+      *reinterpret_cast<uint4*>(row_addr<ES>(p, A, B, t, rr) + (q % PPR) * 16) =
+          *reinterpret_cast<const uint4*>(src + q * 16);
+  }
+}
+
+// 8 consecutive values (bf16 or fp32) from shared memory.
+template <int ES>
+__device__ __forceinline__ void lds8(const uint8_t* src, float (&x)[kHPL]) {
+  if (ES == 2) {
+    const uint4 w = *reinterpret_cast<const uint4*>(src);
+    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ww[i]));
-        x[2 * i] = f.x, x[2 * i + 1] = f.y;
-      }
-    } else {
-      const float4* f4 = reinterpret_cast<const float4*>(src + h * kHPL * 4);
-      const float4 a = f4[0], b = f4[1];
-      x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ww[i]));
+      x[2 * i] = f.x, x[2 * i + 1] = f.y;
     }
+  } else {
+    const float4 a = reinterpret_cast<const float4*>(src)[0], b = reinterpret_cast<const float4*>(src)[1];
+    x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
   }
 }
 
-__device__ __forceinline__ void store_half(void* base, int64_t off, bool is_bf16, const float (&y)[kHPL]) {
-  if (is_bf16) {
-    uint4 w;
-    w.x = pack_bf16(y[0], y[1]);
-    w.y = pack_bf16(y[2], y[3]);
-    w.z = pack_bf16(y[4], y[5]);
-    w.w = pack_bf16(y[6], y[7]);
-    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(base) + off) = w;
+template <int ES>
+__device__ __forceinline__ void sts8(uint8_t* dst, const float (&y)[kHPL]) {
+  if (ES == 2) {
+    *reinterpret_cast<uint4*>(dst) =
+        make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
   } else {
-    float4* p = reinterpret_cast<float4*>(static_cast<float*>(base) + off);
-    p[0] = make_float4(y[0], y[1], y[2], y[3]);
-    p[1] = make_float4(y[4], y[5], y[6], y[7]);
+    reinterpret_cast<float4*>(dst)[0] = make_float4(y[0], y[1], y[2], y[3]);
+    reinterpret_cast<float4*>(dst)[1] = make_float4(y[4], y[5], y[6], y[7]);
   }
 }
 
@@ -136,19 +163,52 @@ __device__ __forceinline__ bool warp_find_sequence(const QkPrepParams& p, int64_
 
 // cos/sin of this lane's 8 frequencies at position pos, formed as the reference
 // forms its table: fp32 t*f, or (bf16 mode) t, f and t*f rounded to bf16 and
-// cos/sin rounded to bf16.
-__device__ __forceinline__ void rope_table(const QkPrepParams& p, int pos, int sub, float (&c)[kHPL],
-                                           float (&s)[kHPL]) {
+// cos/sin rounded to bf16.  The RPW row groups of a warp need the same values,
+// so each lane evaluates VPL = 8/RPW of them (frequencies fr, preloaded) and
+// the warp exchanges them; all lanes must call this together.
+template <int LPR, int VPL>
+__device__ __forceinline__ void rope_table(bool bf16_mode, int pos, int sub, const float (&fr)[VPL],
+                                           float (&c)[kHPL], float (&s)[kHPL]) {
+  float cm[VPL], sm[VPL];
 #pragma unroll
-  for (int v = 0; v < kHPL; ++v) {
-    const float f = __ldg(p.inv_freq + kHPL * sub + v), t = static_cast<float>(pos);
-    const float ang = p.rope_bf16 ? bf16_round(bf16_round(t) * bf16_round(f)) : t * f;
-    sincosf(ang, &s[v], &c[v]);
-    if (p.rope_bf16) {
-      c[v] = bf16_round(c[v]);
-      s[v] = bf16_round(s[v]);
+  for (int i = 0; i < VPL; ++i) {
+    const float t = static_cast<float>(pos);
+    const float ang = bf16_mode ? bf16_round(bf16_round(t) * bf16_round(fr[i])) : t * fr[i];
+    sincosf(ang, &sm[i], &cm[i]);
+    if (bf16_mode) {
+      cm[i] = bf16_round(cm[i]);
+      sm[i] = bf16_round(sm[i]);
     }
   }
+#pragma unroll
+  for (int v = 0; v < kHPL; ++v) {  // entry v of this lane's columns sits in row group v / VPL
+    c[v] = __shfl_sync(0xffffffffu, cm[v % VPL], (v / VPL) * LPR + sub);
+    s[v] = __shfl_sync(0xffffffffu, sm[v % VPL], (v / VPL) * LPR + sub);
+  }
+}
+
+__device__ __forceinline__ uint32_t bf162_bits(__nv_bfloat162 h) { return *reinterpret_cast<const uint32_t*>(&h); }
+
+// y1 = x1*c + (-x2)*s and y2 = x2*c + x1*s on bf16 operands with the reference's
+// roundings (each product rounded to bf16, then the sum), written as packed
+// bf16 words.  Each bf16 product is exact in fp32 and a sum of two bf16 values
+// rounds to the same bf16 whether or not it passes through fp32 first, so
+// bf16x2 arithmetic reproduces the reference's fp32-computed bf16 ops.
+__device__ __forceinline__ void rope_bf16_packed(const float (&x1)[kHPL], const float (&x2)[kHPL],
+                                                 const float (&c)[kHPL], const float (&s)[kHPL], uint4& y1,
+                                                 uint4& y2) {
+  uint32_t o1[4], o2[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(x1[2 * i], x1[2 * i + 1]);
+    const __nv_bfloat162 b = __floats2bfloat162_rn(x2[2 * i], x2[2 * i + 1]);
+    const __nv_bfloat162 cc = __floats2bfloat162_rn(c[2 * i], c[2 * i + 1]);
+    const __nv_bfloat162 sn = __floats2bfloat162_rn(s[2 * i], s[2 * i + 1]);
+    o1[i] = bf162_bits(__hsub2(__hmul2_rn(a, cc), __hmul2_rn(b, sn)));
+    o2[i] = bf162_bits(__hadd2(__hmul2_rn(b, cc), __hmul2_rn(a, sn)));
+  }
+  y1 = make_uint4(o1[0], o1[1], o1[2], o1[3]);
+  y2 = make_uint4(o2[0], o2[1], o2[2], o2[3]);
 }
 
 template <int LPR, int N>
@@ -159,31 +219,32 @@ __device__ __forceinline__ void row_sums(float (&v)[N]) {
     for (int j = 0; j < N; ++j) v[j] += __shfl_xor_sync(0xffffffffu, v[j], o);
 }
 
-// Shared-memory layout of both directions: the two RMSNorm weights (fp32) and,
-// per warp, kPrepStages units of row batches (x, and dy for the backward).
-inline size_t qk_prep_smem(int D, int in_bytes, bool bwd) {
-  const int rows_per_unit = (bwd ? kRowBatchBwd : kRowBatch) * 32 / (D / (2 * kHPL));
-  return static_cast<size_t>(2 * D * 4) + static_cast<size_t>(kPrepThreads / 32) * kPrepStages * rows_per_unit * D *
-                                              in_bytes * (bwd ? 2 : 1);
+// Rows per streamed unit and the unit's bytes: operand 0 (x, or dy for the
+// backward, bf16) then operand 1 (the backward's x).
+constexpr int qk_unit_rows(int D, bool bwd, int eb) { return (bwd || eb == 4 ? 1 : 2) * (32 / (D / (2 * kHPL))); }
+constexpr int qk_unit_bytes(int D, bool bwd, int eb) {
+  return qk_unit_rows(D, bwd, eb) * D * (bwd ? 2 + eb : eb);
+}
+
+// Shared memory: the two RMSNorm weights (fp32), then kPrepStages units per warp.
+constexpr size_t qk_prep_smem(int D, bool bwd, int eb) {
+  return static_cast<size_t>(2 * D * 4) + static_cast<size_t>(kPrepThreads / 32) * kPrepStages * qk_unit_bytes(D, bwd, eb);
 }
 
 // One kernel for both directions: BWD reads x and dy and writes dx (+ weight
-// gradients); the forward reads x and writes y.
-template <int D, bool BWD>
-__global__ void __launch_bounds__(kPrepThreads) fna2_qk_prep_kernel(const QkPrepParams p) {
+// gradients); the forward reads x and writes y.  EB: bytes per input element.
+template <int D, bool BWD, int EB>
+__global__ void __launch_bounds__(kPrepThreads, BWD ? 2 : 3) fna2_qk_prep_kernel(const QkPrepParams p) {
   constexpr int LPR = D / (2 * kHPL), RPW = 32 / LPR;
-  constexpr int RBATCH = BWD ? kRowBatchBwd : kRowBatch;
-  constexpr int RB = RPW * RBATCH;                 // rows per streamed unit
-  constexpr int OPS = BWD ? 2 : 1;
+  constexpr int RB = qk_unit_rows(D, BWD, EB), RBATCH = RB / RPW;  // rows, row batches per unit
+  constexpr int E0 = BWD ? 2 : EB;                                  // bytes per element of operand 0
+  constexpr int B0 = RB * D * E0, UNIT = qk_unit_bytes(D, BWD, EB);
   extern __shared__ __align__(16) uint8_t prep_smem[];
   float* s_w = reinterpret_cast<float*>(prep_smem);  // [2][D]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sub = lane % LPR, rsel = lane / LPR;
   const bool rope = p.inv_freq != nullptr, norm = p.qw != nullptr;
   const int rows = p.hq + p.hk, units_per_token = (rows + RB - 1) / RB;
-  const int in_bytes = p.in_bf16 ? 2 : 4;
-  const int row_bytes = D * in_bytes;                 // one row of one operand, all lanes of the row
-  const int unit_bytes = RB * row_bytes * OPS;
-  uint8_t* wbuf = prep_smem + 2 * D * 4 + static_cast<size_t>(warp) * kPrepStages * unit_bytes;
+  uint8_t* wbuf = prep_smem + 2 * D * 4 + static_cast<size_t>(warp) * kPrepStages * UNIT;
   if (norm)
     for (int e = threadIdx.x; e < 2 * D; e += kPrepThreads) {
       const void* w = e < D ? p.qw : p.kw;
@@ -200,56 +261,57 @@ __global__ void __launch_bounds__(kPrepThreads) fna2_qk_prep_kernel(const QkPrep
   const int64_t chunk = (p.T + nw - 1) / nw;
   const int64_t run_beg = gw * chunk, run_end = min(p.T, run_beg + chunk);
   const int64_t n_units = run_end > run_beg ? (run_end - run_beg) * units_per_token : 0;
-  // lane slot of row batch j within a unit: [operand][j][lane] pieces of 2*kHPL values
-  auto slot = [&](uint8_t* st, int op, int j) { return st + ((op * RBATCH + j) * 32 + lane) * 2 * kHPL * in_bytes; };
-  auto issue = [&](int64_t u) {
-    if (u < n_units) {
-      const int64_t t = run_beg + u / units_per_token;
-      const int b = static_cast<int>(u % units_per_token);
-      uint8_t* st = wbuf + (u % kPrepStages) * unit_bytes;
-#pragma unroll
-      for (int j = 0; j < RBATCH; ++j) {
-        const int r = b * RB + j * RPW + rsel;
-        const bool valid = r < rows, isq = r < p.hq;
-        const int hh = isq ? r : r - p.hq;
-        if (BWD) {
-          const QkRows& go = isq ? p.dqo : p.dko;
-          stage_row(slot(st, 0, j), go.ptr, t * go.ts + hh * go.hs, D, sub, 2, valid);
-          if (norm) {
-            const QkRows& in = isq ? p.qi : p.ki;
-            stage_row(slot(st, 1, j), in.ptr, t * in.ts + hh * in.hs, D, sub, in_bytes, valid);
-          }
-        } else {
-          const QkRows& in = isq ? p.qi : p.ki;
-          stage_row(slot(st, 0, j), in.ptr, t * in.ts + hh * in.hs, D, sub, in_bytes, valid);
-        }
+  // cursors (token, unit within the token) of the next unit to stage and to consume
+  int64_t issue_n = 0, issue_t = run_beg, use_t = run_beg;
+  int issue_b = 0, use_b = 0;
+  auto issue = [&]() {
+    if (issue_n < n_units) {
+      uint8_t* st = wbuf + (issue_n % kPrepStages) * UNIT;
+      if (BWD) {
+        stage_rows<D, RB, 2>(st, p, p.dqo, p.dko, issue_t, issue_b * RB, lane);
+        if (norm) stage_rows<D, RB, EB>(st + B0, p, p.qi, p.ki, issue_t, issue_b * RB, lane);
+      } else {
+        stage_rows<D, RB, EB>(st, p, p.qi, p.ki, issue_t, issue_b * RB, lane);
       }
+      if (++issue_b == units_per_token) issue_b = 0, ++issue_t;
+      ++issue_n;
     }
     cp_async_commit();
   };
 #pragma unroll
-  for (int u = 0; u < kPrepStages - 1; ++u) issue(u);
+  for (int u = 0; u < kPrepStages - 1; ++u) issue();
   int s_lo = 0, s_hi = 0;
   bool inside = true;
   float c[kHPL], s[kHPL];
+  constexpr int VPL = kHPL / RPW;
+  float fr[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) fr[i] = rope ? __ldg(p.inv_freq + kHPL * sub + rsel * VPL + i) : 0.f;
   for (int64_t u = 0; u < n_units; ++u) {
-    issue(u + kPrepStages - 1);
-    cp_async_wait<kPrepStages - 1>();  // unit u has landed
-    const int64_t t = run_beg + u / units_per_token;
-    const int b = static_cast<int>(u % units_per_token);
+    __syncwarp();  // every lane is done with the slot that this issue refills
+    issue();
+    cp_async_wait<kPrepStages - 1>();  // this lane's pieces of unit u have landed
+    __syncwarp();                      // and so have the other lanes'
+    const int64_t t = use_t;
+    const int b = use_b;
+    if (++use_b == units_per_token) use_b = 0, ++use_t;
     if (b == 0 && rope) {  // a new token: its position and cos/sin
       if (t < s_lo || t >= s_hi) {
         inside = warp_find_sequence(p, t, lane, &s_lo, &s_hi);
         if (!inside) s_lo = s_hi = 0;
       }
-      if (inside) rope_table(p, static_cast<int>(t - s_lo), sub, c, s);
+      if (inside) rope_table<LPR, VPL>(p.rope_bf16, static_cast<int>(t - s_lo), sub, fr, c, s);
     }
-    uint8_t* st = wbuf + (u % kPrepStages) * unit_bytes;
+    uint8_t* st = wbuf + (u % kPrepStages) * UNIT;
     if (!BWD) {
       if (rope && !inside) continue;  // outside every sequence: left unset, as the reference does
       float x1[RBATCH][kHPL], x2[RBATCH][kHPL], ss[RBATCH];
 #pragma unroll
-      for (int j = 0; j < RBATCH; ++j) unstage_row(slot(st, 0, j), p.in_bf16, x1[j], x2[j]);
+      for (int j = 0; j < RBATCH; ++j) {
+        const uint8_t* rp = st + (j * RPW + rsel) * D * EB;
+        lds8<EB>(rp + kHPL * sub * EB, x1[j]);
+        lds8<EB>(rp + (D / 2 + kHPL * sub) * EB, x2[j]);
+      }
       if (norm) {
 #pragma unroll
         for (int j = 0; j < RBATCH; ++j) {
@@ -259,10 +321,10 @@ __global__ void __launch_bounds__(kPrepThreads) fna2_qk_prep_kernel(const QkPrep
         }
         row_sums<LPR>(ss);
       }
+      if (EB != 2) __syncwarp();  // the bf16 output rows overlap other lanes' fp32 input pieces
 #pragma unroll
       for (int j = 0; j < RBATCH; ++j) {
-        const int r = b * RB + j * RPW + rsel;
-        const bool isq = r < p.hq;
+        const bool isq = b * RB + j * RPW + rsel < p.hq;
         if (norm) {
           const float rho = rsqrtf(ss[j] * (1.f / D) + p.eps);
           const float* w = s_w + (isq ? 0 : D);
@@ -272,34 +334,40 @@ __global__ void __launch_bounds__(kPrepThreads) fna2_qk_prep_kernel(const QkPrep
             x2[j][v] = x2[j][v] * rho * w[D / 2 + kHPL * sub + v];
           }
         }
+        uint8_t* op = st + (j * RPW + rsel) * D * 2;
+        if (rope && p.rope_bf16) {
+          uint4 y1, y2;
+          rope_bf16_packed(x1[j], x2[j], c, s, y1, y2);
+          *reinterpret_cast<uint4*>(op + kHPL * sub * 2) = y1;
+          *reinterpret_cast<uint4*>(op + (D / 2 + kHPL * sub) * 2) = y2;
+          continue;
+        }
         if (rope) {
 #pragma unroll
-          for (int v = 0; v < kHPL; ++v) {  // y1 = x1 c - x2 s, y2 = x2 c + x1 s
+          for (int v = 0; v < kHPL; ++v) {  // fp32: y1 = x1 c + (-x2) s, y2 = x2 c + x1 s, uncontracted
             const float a = x1[j][v], bb = x2[j][v];
-            if (p.rope_bf16) {
-              const float ab = bf16_round(a), bbb = bf16_round(bb);
-              x1[j][v] = bf16_round(ab * c[v]) + bf16_round(-bbb * s[v]);
-              x2[j][v] = bf16_round(bbb * c[v]) + bf16_round(ab * s[v]);
-            } else {
-              x1[j][v] = a * c[v] - bb * s[v];
-              x2[j][v] = bb * c[v] + a * s[v];
-            }
+            x1[j][v] = __fadd_rn(__fmul_rn(a, c[v]), -__fmul_rn(bb, s[v]));
+            x2[j][v] = __fadd_rn(__fmul_rn(bb, c[v]), __fmul_rn(a, s[v]));
           }
         }
-        if (r < rows) {
-          const QkRows& out = isq ? p.qo : p.ko;
-          const int64_t off = t * out.ts + (isq ? r : r - p.hq) * out.hs + kHPL * sub;
-          store_half(out.ptr, off, true, x1[j]);
-          store_half(out.ptr, off + D / 2, true, x2[j]);
-        }
+        sts8<2>(op + kHPL * sub * 2, x1[j]);
+        sts8<2>(op + (D / 2 + kHPL * sub) * 2, x2[j]);
       }
+      __syncwarp();
+      store_rows<D, RB, 2>(st, p, p.qo, p.ko, t, b * RB, lane);
     } else {
       const bool zero = rope && !inside;  // outside every sequence: no path to the output
       float g1[RBATCH][kHPL], g2[RBATCH][kHPL], x1[RBATCH][kHPL], x2[RBATCH][kHPL];
 #pragma unroll
       for (int j = 0; j < RBATCH; ++j) {
-        unstage_row(slot(st, 0, j), true, g1[j], g2[j]);
-        if (norm) unstage_row(slot(st, 1, j), p.in_bf16, x1[j], x2[j]);
+        const uint8_t* gp = st + (j * RPW + rsel) * D * 2;
+        lds8<2>(gp + kHPL * sub * 2, g1[j]);
+        lds8<2>(gp + (D / 2 + kHPL * sub) * 2, g2[j]);
+        if (norm) {
+          const uint8_t* xp = st + B0 + (j * RPW + rsel) * D * EB;
+          lds8<EB>(xp + kHPL * sub * EB, x1[j]);
+          lds8<EB>(xp + (D / 2 + kHPL * sub) * EB, x2[j]);
+        }
       }
       if (rope && !zero) {
 #pragma unroll
@@ -350,20 +418,19 @@ __global__ void __launch_bounds__(kPrepThreads) fna2_qk_prep_kernel(const QkPrep
           }
         }
       }
+      // dx goes where this lane read its x pieces (operand 1, same element size)
 #pragma unroll
       for (int j = 0; j < RBATCH; ++j) {
-        const int r = b * RB + j * RPW + rsel;
-        if (r >= rows) continue;
         if (zero) {
 #pragma unroll
           for (int v = 0; v < kHPL; ++v) g1[j][v] = g2[j][v] = 0.f;
         }
-        const bool isq = r < p.hq;
-        const QkRows& gin = isq ? p.dqi : p.dki;
-        const int64_t off = t * gin.ts + (isq ? r : r - p.hq) * gin.hs + kHPL * sub;
-        store_half(gin.ptr, off, p.in_bf16, g1[j]);
-        store_half(gin.ptr, off + D / 2, p.in_bf16, g2[j]);
+        uint8_t* xp = st + B0 + (j * RPW + rsel) * D * EB;
+        sts8<EB>(xp + kHPL * sub * EB, g1[j]);
+        sts8<EB>(xp + (D / 2 + kHPL * sub) * EB, g2[j]);
       }
+      __syncwarp();
+      store_rows<D, RB, EB>(st + B0, p, p.dqi, p.dki, t, b * RB, lane);
     }
   }
   cp_async_wait<0>();
@@ -400,13 +467,14 @@ __global__ void __launch_bounds__(kPrepThreads) fna2_qk_prep_kernel(const QkPrep
   }
 }
 
-template <int D, bool BWD>
+template <int D, bool BWD, int EB>
 cudaError_t launch_qk_prep_t(const QkPrepParams& p, cudaStream_t stream) {
-  auto kern = fna2_qk_prep_kernel<D, BWD>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(qk_prep_smem(D, 4, BWD)));
+  auto kern = fna2_qk_prep_kernel<D, BWD, EB>;
+  constexpr size_t smem = qk_prep_smem(D, BWD, EB);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) return e;
-  const size_t smem = qk_prep_smem(D, p.in_bf16 ? 2 : 4, BWD);
   int dev = 0, sms = 148, per_sm = 1;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -421,8 +489,15 @@ cudaError_t launch_qk_prep_t(const QkPrepParams& p, cudaStream_t stream) {
 }
 
 cudaError_t launch_qk_prep(const QkPrepParams& p, int D, bool bwd, cudaStream_t stream) {
-  if (D == 128) return bwd ? launch_qk_prep_t<128, true>(p, stream) : launch_qk_prep_t<128, false>(p, stream);
-  if (D == 64) return bwd ? launch_qk_prep_t<64, true>(p, stream) : launch_qk_prep_t<64, false>(p, stream);
+  const bool b16 = p.in_bf16 != 0;
+  if (D == 128) {
+    if (bwd) return b16 ? launch_qk_prep_t<128, true, 2>(p, stream) : launch_qk_prep_t<128, true, 4>(p, stream);
+    return b16 ? launch_qk_prep_t<128, false, 2>(p, stream) : launch_qk_prep_t<128, false, 4>(p, stream);
+  }
+  if (D == 64) {
+    if (bwd) return b16 ? launch_qk_prep_t<64, true, 2>(p, stream) : launch_qk_prep_t<64, true, 4>(p, stream);
+    return b16 ? launch_qk_prep_t<64, false, 2>(p, stream) : launch_qk_prep_t<64, false, 4>(p, stream);
+  }
   return cudaErrorInvalidValue;
 }
 
