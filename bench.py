@@ -376,11 +376,14 @@ def run_qk_prep(args, w):
     k = torch.randn(T, H, D, device=dev, generator=g).bfloat16().requires_grad_(True)
     norms = [types.SimpleNamespace(weight=torch.ones(D, device=dev, dtype=torch.bfloat16).requires_grad_(True),
                                    eps=1e-6) for _ in range(2)]
-    rope = types.SimpleNamespace(inv_freq=QO.rope_inv_freq(D))
+    rope = types.SimpleNamespace(inv_freq=QO.rope_inv_freq(D).to(dev))
     gq = torch.randn(T, H, D, device=dev, generator=g).bfloat16()
     gk = torch.randn(T, H, D, device=dev, generator=g).bfloat16()
 
     def step():
+        # gradients set to None between steps (zero_grad(set_to_none=True)), so
+        # autograd hands over dq/dk instead of adding them into earlier ones
+        q.grad = k.grad = norms[0].weight.grad = norms[1].weight.grad = None
         qo, ko = apply_qk_norm_rope_varlen(q, k, cu, norms[0], norms[1], rope)
         torch.autograd.backward([qo, ko], [gq, gk])
 

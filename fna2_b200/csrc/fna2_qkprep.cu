@@ -63,7 +63,9 @@ __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(_
 // RoPE needs no shuffles; row sums reduce over the row's LPR lanes.  A warp
 // covers RPW = 32/LPR rows per row batch.
 constexpr int kHPL = 8;         // values per lane per half row
-constexpr int kPrepStages = 4;  // units in flight per warp
+// Units in flight per warp.  The backward runs two CTAs per SM (its registers),
+// so it keeps more units in flight per warp.
+constexpr int qk_stages(bool bwd) { return bwd ? 4 : 4; }
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(valid ? 16 : 0)
@@ -82,13 +84,34 @@ __device__ __forceinline__ uint8_t* row_addr(const QkPrepParams& p, const QkRows
   return static_cast<uint8_t*>(m.ptr) + (t * m.ts + static_cast<int64_t>(isq ? rr : rr - p.hq) * m.hs) * ES;
 }
 
+// First byte of this lane's first piece when global rows [row0, row0 + RB) of
+// token t all belong to one tensor (A: rows < hq, B: the rest) and all exist;
+// nullptr otherwise.  *step: bytes between a lane's consecutive pieces.
+template <int D, int RB, int ES>
+__device__ __forceinline__ uint8_t* unit_rows(const QkPrepParams& p, const QkRows& A, const QkRows& B, int64_t t,
+                                              int row0, int lane, int64_t* step) {
+  constexpr int PPR = D * ES / 16;  // 16-byte pieces per row (8, 16 or 32)
+  const bool in_a = row0 + RB <= p.hq, in_b = row0 >= p.hq && row0 + RB <= p.hq + p.hk;
+  if (!in_a && !in_b) return nullptr;
+  const QkRows m = pick(in_a, A, B);
+  *step = (32 / PPR) * m.hs * ES;
+  return static_cast<uint8_t*>(m.ptr) + (t * m.ts + static_cast<int64_t>(in_a ? row0 : row0 - p.hq) * m.hs) * ES +
+         (lane / PPR) * m.hs * ES + (lane % PPR) * 16;
+}
+
 // Copy global rows [row0, row0 + RB) of token t into a row-major block at dst
 // (rows past hq + hk are zero-filled).
 template <int D, int RB, int ES>
 __device__ __forceinline__ void stage_rows(uint8_t* dst, const QkPrepParams& p, const QkRows& A, const QkRows& B,
                                            int64_t t, int row0, int lane) {
-  constexpr int PPR = D * ES / 16;  // 16-byte pieces per row
-  static_assert((RB * PPR) % 32 == 0, "a unit is whole warp instructions");
+  constexpr int PPR = D * ES / 16;
+  static_assert((RB * PPR) % 32 == 0 && PPR <= 32, "a unit is whole warp instructions");
+  int64_t step = 0;
+  if (const uint8_t* g = unit_rows<D, RB, ES>(p, A, B, t, row0, lane, &step)) {
+#pragma unroll
+    for (int i = 0; i < RB * PPR / 32; ++i) cp_async16(dst + (i * 32 + lane) * 16, g + i * step, true);
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < RB * PPR / 32; ++i) {
     const int q = i * 32 + lane, rr = row0 + q / PPR;
@@ -103,6 +126,13 @@ template <int D, int RB, int ES>
 __device__ __forceinline__ void store_rows(const uint8_t* src, const QkPrepParams& p, const QkRows& A,
                                            const QkRows& B, int64_t t, int row0, int lane) {
   constexpr int PPR = D * ES / 16;
+  int64_t step = 0;
+  if (uint8_t* g = unit_rows<D, RB, ES>(p, A, B, t, row0, lane, &step)) {
+#pragma unroll
+    for (int i = 0; i < RB * PPR / 32; ++i)
+      *reinterpret_cast<uint4*>(g + i * step) = *reinterpret_cast<const uint4*>(src + (i * 32 + lane) * 16);
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < RB * PPR / 32; ++i) {
     const int q = i * 32 + lane, rr = row0 + q / PPR;
@@ -226,9 +256,9 @@ constexpr int qk_unit_bytes(int D, bool bwd, int eb) {
   return qk_unit_rows(D, bwd, eb) * D * (bwd ? 2 + eb : eb);
 }
 
-// Shared memory: the two RMSNorm weights (fp32), then kPrepStages units per warp.
+// Shared memory: the two RMSNorm weights (fp32), then the units of each warp's ring.
 constexpr size_t qk_prep_smem(int D, bool bwd, int eb) {
-  return static_cast<size_t>(2 * D * 4) + static_cast<size_t>(kPrepThreads / 32) * kPrepStages * qk_unit_bytes(D, bwd, eb);
+  return static_cast<size_t>(2 * D * 4) + static_cast<size_t>(kPrepThreads / 32) * qk_stages(bwd) * qk_unit_bytes(D, bwd, eb);
 }
 
 // One kernel for both directions: BWD reads x and dy and writes dx (+ weight
@@ -238,7 +268,7 @@ __global__ void __launch_bounds__(kPrepThreads, BWD ? 2 : 3) fna2_qk_prep_kernel
   constexpr int LPR = D / (2 * kHPL), RPW = 32 / LPR;
   constexpr int RB = qk_unit_rows(D, BWD, EB), RBATCH = RB / RPW;  // rows, row batches per unit
   constexpr int E0 = BWD ? 2 : EB;                                  // bytes per element of operand 0
-  constexpr int B0 = RB * D * E0, UNIT = qk_unit_bytes(D, BWD, EB);
+  constexpr int B0 = RB * D * E0, UNIT = qk_unit_bytes(D, BWD, EB), kPrepStages = qk_stages(BWD);
   extern __shared__ __align__(16) uint8_t prep_smem[];
   float* s_w = reinterpret_cast<float*>(prep_smem);  // [2][D]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sub = lane % LPR, rsel = lane / LPR;

@@ -78,3 +78,25 @@ def test_tokens_after_last_sequence_get_zero_gradient():
     q, k, wq, wk, inv, cu, dqo, dko = Q.make_inputs([10, 20], 2, 2, 128, 5, tail=6)
     _, _, gq, gk, _, _ = _run(q, k, cu, wq, wk, 1e-6, inv, dqo, dko)
     assert (gq[30:] == 0).all() and (gk[30:] == 0).all()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("D", [64, 128])
+def test_many_heads_strided_views_vs_oracle(D, dtype):
+    """16 query and 8 key heads, so units of rows fall wholly inside q or k, and
+    q, k as head slices of one packed qkv tensor (token stride != heads * D)."""
+    H, H_KV, lengths = 16, 8, [300, 5, 1000, 1]
+    T = sum(lengths)
+    g = torch.Generator().manual_seed(40 + D)
+    qkv = torch.randn(T, H + 2 * H_KV, D, generator=g).to(dtype).cuda()
+    q, k = qkv[:, :H], qkv[:, H:H + H_KV]
+    assert q.stride(0) == (H + 2 * H_KV) * D
+    _, _, wq, wk, inv, cu, _, _ = Q.make_inputs(lengths, H, H_KV, D, 41 + D, dtype)
+    dqo = torch.randn(T, H, D, generator=g).bfloat16()
+    dko = torch.randn(T, H_KV, D, generator=g).bfloat16()
+    qo, ko, gq, gk, gwq, gwk = _run(q, k, cu, wq, wk, 1e-6, inv, dqo, dko)
+    rq, rk, grads = Q.qk_prep_with_grads(q.cpu().contiguous(), k.cpu().contiguous(), cu, wq, wk, 1e-6, inv, dqo, dko)
+    _close("q_out", qo, rq)
+    _close("k_out", ko, rk)
+    for n, got, want in zip(("dq", "dk", "dwq", "dwk"), (gq, gk, gwq, gwk), grads):
+        _close(n, got, want)
