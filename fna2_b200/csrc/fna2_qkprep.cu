@@ -63,9 +63,7 @@ __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(_
 // RoPE needs no shuffles; row sums reduce over the row's LPR lanes.  A warp
 // covers RPW = 32/LPR rows per row batch.
 constexpr int kHPL = 8;         // values per lane per half row
-// Units in flight per warp.  The backward runs two CTAs per SM (its registers),
-// so it keeps more units in flight per warp.
-constexpr int qk_stages(bool bwd) { return bwd ? 4 : 4; }
+constexpr int kPrepStages = 4;  // units in flight per warp
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(valid ? 16 : 0)
@@ -241,6 +239,25 @@ __device__ __forceinline__ void rope_bf16_packed(const float (&x1)[kHPL], const 
   y2 = make_uint4(o2[0], o2[1], o2[2], o2[3]);
 }
 
+// RMSNorm weights in shared memory are stored so that the lanes of a row read
+// 16 consecutive bytes each (no bank conflicts): column e of half h sits in
+// float4 slot (h * 2 + (e % 8) / 4) * LPR + e / 8, component e % 4.
+template <int D>
+__device__ __forceinline__ int w_slot(int col) {
+  constexpr int LPR = D / (2 * kHPL);
+  const int h = col / (D / 2), e = col % (D / 2);
+  return ((h * 2 + (e % kHPL) / 4) * LPR + e / kHPL) * 4 + e % 4;
+}
+
+template <int D>
+__device__ __forceinline__ void load_w(const float* sw, int sub, float (&w1)[kHPL], float (&w2)[kHPL]) {
+  constexpr int LPR = D / (2 * kHPL);
+  const float4* w4 = reinterpret_cast<const float4*>(sw);
+  const float4 a = w4[sub], b = w4[LPR + sub], c = w4[2 * LPR + sub], d = w4[3 * LPR + sub];
+  w1[0] = a.x, w1[1] = a.y, w1[2] = a.z, w1[3] = a.w, w1[4] = b.x, w1[5] = b.y, w1[6] = b.z, w1[7] = b.w;
+  w2[0] = c.x, w2[1] = c.y, w2[2] = c.z, w2[3] = c.w, w2[4] = d.x, w2[5] = d.y, w2[6] = d.z, w2[7] = d.w;
+}
+
 template <int LPR, int N>
 __device__ __forceinline__ void row_sums(float (&v)[N]) {
 #pragma unroll
@@ -258,7 +275,7 @@ constexpr int qk_unit_bytes(int D, bool bwd, int eb) {
 
 // Shared memory: the two RMSNorm weights (fp32), then the units of each warp's ring.
 constexpr size_t qk_prep_smem(int D, bool bwd, int eb) {
-  return static_cast<size_t>(2 * D * 4) + static_cast<size_t>(kPrepThreads / 32) * qk_stages(bwd) * qk_unit_bytes(D, bwd, eb);
+  return static_cast<size_t>(2 * D * 4) + static_cast<size_t>(kPrepThreads / 32) * kPrepStages * qk_unit_bytes(D, bwd, eb);
 }
 
 // One kernel for both directions: BWD reads x and dy and writes dx (+ weight
@@ -268,9 +285,9 @@ __global__ void __launch_bounds__(kPrepThreads, BWD ? 2 : 3) fna2_qk_prep_kernel
   constexpr int LPR = D / (2 * kHPL), RPW = 32 / LPR;
   constexpr int RB = qk_unit_rows(D, BWD, EB), RBATCH = RB / RPW;  // rows, row batches per unit
   constexpr int E0 = BWD ? 2 : EB;                                  // bytes per element of operand 0
-  constexpr int B0 = RB * D * E0, UNIT = qk_unit_bytes(D, BWD, EB), kPrepStages = qk_stages(BWD);
+  constexpr int B0 = RB * D * E0, UNIT = qk_unit_bytes(D, BWD, EB);
   extern __shared__ __align__(16) uint8_t prep_smem[];
-  float* s_w = reinterpret_cast<float*>(prep_smem);  // [2][D]
+  float* s_w = reinterpret_cast<float*>(prep_smem);  // [2][D], columns placed by w_slot
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sub = lane % LPR, rsel = lane / LPR;
   const bool rope = p.inv_freq != nullptr, norm = p.qw != nullptr;
   const int rows = p.hq + p.hk, units_per_token = (rows + RB - 1) / RB;
@@ -279,7 +296,7 @@ __global__ void __launch_bounds__(kPrepThreads, BWD ? 2 : 3) fna2_qk_prep_kernel
     for (int e = threadIdx.x; e < 2 * D; e += kPrepThreads) {
       const void* w = e < D ? p.qw : p.kw;
       const int i = e % D;
-      s_w[e] = p.w_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(w)[i]) : static_cast<const float*>(w)[i];
+      s_w[(e / D) * D + w_slot<D>(i)] = p.w_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(w)[i]) : static_cast<const float*>(w)[i];
     }
   __syncthreads();
   float gq1[kHPL], gq2[kHPL], gk1[kHPL], gk2[kHPL];  // weight gradients (backward)
@@ -357,11 +374,12 @@ __global__ void __launch_bounds__(kPrepThreads, BWD ? 2 : 3) fna2_qk_prep_kernel
         const bool isq = b * RB + j * RPW + rsel < p.hq;
         if (norm) {
           const float rho = rsqrtf(ss[j] * (1.f / D) + p.eps);
-          const float* w = s_w + (isq ? 0 : D);
+          float w1[kHPL], w2[kHPL];
+          load_w<D>(s_w + (isq ? 0 : D), sub, w1, w2);
 #pragma unroll
           for (int v = 0; v < kHPL; ++v) {
-            x1[j][v] = x1[j][v] * rho * w[kHPL * sub + v];
-            x2[j][v] = x2[j][v] * rho * w[D / 2 + kHPL * sub + v];
+            x1[j][v] = x1[j][v] * rho * w1[v];
+            x2[j][v] = x2[j][v] * rho * w2[v];
           }
         }
         uint8_t* op = st + (j * RPW + rsel) * D * 2;
@@ -414,13 +432,13 @@ __global__ void __launch_bounds__(kPrepThreads, BWD ? 2 : 3) fna2_qk_prep_kernel
 #pragma unroll
         for (int j = 0; j < RBATCH; ++j) {
           const bool isq = b * RB + j * RPW + rsel < p.hq;
-          const float* w = s_w + (isq ? 0 : D);
+          float w1[kHPL], w2[kHPL];
+          load_w<D>(s_w + (isq ? 0 : D), sub, w1, w2);
           ss[j] = dot[j] = 0.f;
 #pragma unroll
           for (int v = 0; v < kHPL; ++v) {
             ss[j] = fmaf(x1[j][v], x1[j][v], fmaf(x2[j][v], x2[j][v], ss[j]));
-            dot[j] = fmaf(g1[j][v] * w[kHPL * sub + v], x1[j][v],
-                          fmaf(g2[j][v] * w[D / 2 + kHPL * sub + v], x2[j][v], dot[j]));
+            dot[j] = fmaf(g1[j][v] * w1[v], x1[j][v], fmaf(g2[j][v] * w2[v], x2[j][v], dot[j]));
           }
         }
         row_sums<LPR>(ss);
@@ -429,7 +447,8 @@ __global__ void __launch_bounds__(kPrepThreads, BWD ? 2 : 3) fna2_qk_prep_kernel
         for (int j = 0; j < RBATCH; ++j) {
           const int r = b * RB + j * RPW + rsel;
           const bool isq = r < p.hq;
-          const float* w = s_w + (isq ? 0 : D);
+          float w1[kHPL], w2[kHPL];
+          load_w<D>(s_w + (isq ? 0 : D), sub, w1, w2);
           const float rho = rsqrtf(ss[j] * (1.f / D) + p.eps);
           const float k3 = dot[j] * rho * rho * rho * (1.f / D);
 #pragma unroll
@@ -443,8 +462,8 @@ __global__ void __launch_bounds__(kPrepThreads, BWD ? 2 : 3) fna2_qk_prep_kernel
                 gk2[v] = fmaf(g2[j][v], x2[j][v] * rho, gk2[v]);
               }
             }
-            g1[j][v] = g1[j][v] * w[kHPL * sub + v] * rho - x1[j][v] * k3;
-            g2[j][v] = g2[j][v] * w[D / 2 + kHPL * sub + v] * rho - x2[j][v] * k3;
+            g1[j][v] = g1[j][v] * w1[v] * rho - x1[j][v] * k3;
+            g2[j][v] = g2[j][v] * w2[v] * rho - x2[j][v] * k3;
           }
         }
       }
