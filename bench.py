@@ -21,6 +21,13 @@ threads) on a bounded sample of the same workload.
 (fna2_b200/qk_prep.py) forward + backward on the workload's q and k (bf16,
 H_KV = H), as HBM GB/s against the measured copy bandwidth, with the
 reference's per-sequence CPU path (oracle/qk_prep_oracle.py) timed beside it.
+
+``--op decode`` measures one KV-cache decode step with the relational bias
+(fna2_b200/decode.py) for every sequence of the workload at once: each
+sequence's cache holds its L tokens (packed caches, K/V/R_k), one new token
+per sequence is appended and attends to L + 1 keys; HBM GB/s of the step
+against the measured copy bandwidth, with the decode oracle
+(oracle/decode_oracle.py) timed on the host beside it.
 """
 from __future__ import annotations
 
@@ -441,6 +448,94 @@ def run_qk_prep(args, w):
     }))
 
 
+def run_decode(args, w):
+    """KV-cache decode (one new token per sequence, bias on), one GPU."""
+    from fna2_b200.decode import flash_naylis_decode
+    from oracle import decode_oracle as DO
+    dev = "cuda"
+    lengths, H, D, R = w["lengths"], w["H"], w["D"], w["r"]
+    H_KV = H
+    B = len(lengths)
+    cap = max(lengths) + 1
+    offs = [0]
+    for n in lengths:
+        offs.append(offs[-1] + n + 1)  # each sequence owns L + 1 slots
+    rows = offs[-1]
+    g = torch.Generator(device=dev).manual_seed(0)
+    kc = torch.randn(rows, H_KV, D, device=dev, generator=g, dtype=torch.bfloat16)
+    vc = torch.randn(rows, H_KV, D, device=dev, generator=g, dtype=torch.bfloat16)
+    rkc = (torch.randn(rows, H, R, device=dev, generator=g) * 0.25).bfloat16()
+    q = torch.randn(B, H, D, device=dev, generator=g, dtype=torch.bfloat16)
+    rq = (torch.randn(B, H, R, device=dev, generator=g) * 0.25).bfloat16()
+    kn = torch.randn(B, H_KV, D, device=dev, generator=g, dtype=torch.bfloat16)
+    vn = torch.randn(B, H_KV, D, device=dev, generator=g, dtype=torch.bfloat16)
+    rkn = (torch.randn(B, H, R, device=dev, generator=g) * 0.25).bfloat16()
+    gs = torch.ones(H, device=dev)
+    seq = torch.tensor(lengths, dtype=torch.int32, device=dev)
+    offsets = torch.tensor(offs[:-1], dtype=torch.int32, device=dev)
+
+    def step():
+        return flash_naylis_decode(q, kc, vc, seq, rq, rkc, gs, kn, vn, rkn, cache_offsets=offsets, capacity=cap)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    st = torch.cuda.current_stream()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(0)
+    torch.cuda.synchronize()
+    clocks.start()
+    t0.record(st)
+    for _ in range(args.steps):
+        step()
+    t1.record(st)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    keys = sum(lengths)
+    # reads: cached K, V, R_k of every key, q, r_q, the new rows; writes: the new rows, out
+    algo_bytes = keys * (2 * H_KV * D + H * R) * 2 + B * (H * D + H * R) * 2 + 2 * B * (2 * H_KV * D + H * R) * 2 \
+        + B * H * D * 2
+    gbs = algo_bytes / (ms / 1e3) / 1e9
+    peak, peak_src = None, "measured"
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = json.load(f).get("hbm_gbs")
+    except Exception:
+        pass
+    if peak is None:
+        peak, peak_src = 6650.0, "fallback"
+    cpu = None
+    if not args.no_cpu:
+        torch.set_num_threads(os.cpu_count())
+        sample = [b for b in range(B) if lengths[b] <= 2048][:8]
+        cb = 0
+        qs, rqs = q[sample].cpu(), rq[sample].cpu()
+        kcs = [kc[offs[b]:offs[b] + lengths[b]].cpu() for b in sample]
+        vcs = [vc[offs[b]:offs[b] + lengths[b]].cpu() for b in sample]
+        rks = [rkc[offs[b]:offs[b] + lengths[b]].cpu() for b in sample]
+        Lm = max(lengths[b] for b in sample)
+        pad = lambda ts, x: torch.stack([torch.nn.functional.pad(t, (0, 0, 0, 0, 0, Lm - t.shape[0])) for t in ts])
+        t_c = time.perf_counter()
+        DO.decode(qs, pad(kcs, 0), pad(vcs, 0), [lengths[b] for b in sample], rqs, pad(rks, 0), gs.cpu(),
+                  kn[sample].cpu(), vn[sample].cpu(), rkn[sample].cpu())
+        dt = time.perf_counter() - t_c
+        cb = sum(lengths[b] for b in sample) * (2 * H_KV * D + H * R) * 2
+        cpu = {"value": cb / dt / 1e9, "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"{len(sample)} sequences of the workload with L<=2048 (sum L="
+                         f"{sum(lengths[b] for b in sample)}), fp64 per-head loop, {dt:.2f} s"}
+    print(json.dumps({
+        "metric": "decode step GB/s (KV cache + relational bias, bf16, one new token per sequence)",
+        "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": w["desc"] + f"; decode of one token per sequence against caches of its L tokens, "
+                                           f"H_KV = H = {H}, packed caches", "cached_keys": keys, "sequences": B,
+                   "tokens_per_s": B / (ms / 1e3), "inputs_vs_l2": "caches far larger than L2"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                     "peak_source": peak_src, "algorithmic_bytes_per_step": algo_bytes},
+        "cpu_baseline": cpu, "clocks": clk,
+    }))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -451,11 +546,13 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
-    ap.add_argument("--op", default="attention", choices=["attention", "qk_prep"])
+    ap.add_argument("--op", default="attention", choices=["attention", "qk_prep", "decode"])
     args = ap.parse_args()
     w = workload(args.workload)
     if args.op == "qk_prep":
         run_qk_prep(args, w)
+    elif args.op == "decode":
+        run_decode(args, w)
     elif args.impl == "reference":
         run_reference(args, w)
     else:

@@ -12,14 +12,14 @@ from typing import Optional
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("FNA2_LIB", os.path.join(HERE, "libfna2_b200.so"))
 
-FNA2_ABI_VERSION = 2
+FNA2_ABI_VERSION = 3
 FNA2_OK = 0
 FNA2_ERR_INVALID = -1
 FNA2_ERR_CUDA = -2
 FNA2_ERR_WORKSPACE = -3
 
 EXPORTED = ["fna2_fwd", "fna2_bwd", "fna2_bwd_workspace_size", "fna2_last_error", "fna2_device_status",
-            "fna2_abi_version", "fna2_bwd_noalloc", "fna2_qk_prep_fwd", "fna2_qk_prep_bwd"]
+            "fna2_abi_version", "fna2_bwd_noalloc", "fna2_qk_prep_fwd", "fna2_qk_prep_bwd", "fna2_decode", "fna2_decode_workspace_size"]
 FNA2_DTYPE_F32 = 0
 FNA2_DTYPE_BF16 = 1
 NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024  # FNA2_NOALLOC_SCRATCH_BYTES
@@ -125,6 +125,29 @@ class Fna2QkPrepBwdArgs(ctypes.Structure):
     ]
 
 
+_I64 = ctypes.c_int64
+
+
+class Fna2DecodeArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int), ("heads", ctypes.c_int), ("kv_heads", ctypes.c_int),
+        ("graph_heads", ctypes.c_int), ("head_dim", ctypes.c_int), ("rank", ctypes.c_int),
+        ("capacity", ctypes.c_int), ("softmax_scale", ctypes.c_float),
+        ("q", ctypes.c_void_p), ("q_batch_stride", _I64), ("q_head_stride", _I64),
+        ("r_q", ctypes.c_void_p), ("rq_batch_stride", _I64), ("rq_head_stride", _I64),
+        ("k_cache", ctypes.c_void_p), ("k_batch_stride", _I64), ("k_token_stride", _I64), ("k_head_stride", _I64),
+        ("v_cache", ctypes.c_void_p), ("v_batch_stride", _I64), ("v_token_stride", _I64), ("v_head_stride", _I64),
+        ("rk_cache", ctypes.c_void_p), ("rk_batch_stride", _I64), ("rk_token_stride", _I64),
+        ("rk_head_stride", _I64),
+        ("graph_scale", ctypes.c_void_p), ("cache_seqlens", ctypes.c_void_p), ("cache_offsets", ctypes.c_void_p),
+        ("k_new", ctypes.c_void_p), ("kn_batch_stride", _I64), ("kn_head_stride", _I64),
+        ("v_new", ctypes.c_void_p), ("vn_batch_stride", _I64), ("vn_head_stride", _I64),
+        ("rk_new", ctypes.c_void_p), ("rkn_batch_stride", _I64), ("rkn_head_stride", _I64),
+        ("out", ctypes.c_void_p), ("out_batch_stride", _I64), ("out_head_stride", _I64),
+        ("lse", ctypes.c_void_p), ("num_splits", ctypes.c_int),
+    ]
+
+
 _lib: Optional[ctypes.CDLL] = None
 
 
@@ -148,6 +171,10 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.fna2_qk_prep_fwd.restype = ctypes.c_int
     lib.fna2_qk_prep_bwd.argtypes = [ctypes.POINTER(Fna2QkPrepBwdArgs), ctypes.c_void_p]
     lib.fna2_qk_prep_bwd.restype = ctypes.c_int
+    lib.fna2_decode.argtypes = [ctypes.POINTER(Fna2DecodeArgs), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    lib.fna2_decode.restype = ctypes.c_int
+    lib.fna2_decode_workspace_size.argtypes = [ctypes.POINTER(Fna2DecodeArgs)]
+    lib.fna2_decode_workspace_size.restype = ctypes.c_size_t
     lib.fna2_bwd_workspace_size.argtypes = [ctypes.POINTER(Fna2Problem)]
     lib.fna2_bwd_workspace_size.restype = ctypes.c_size_t
     lib.fna2_last_error.argtypes = []

@@ -7,7 +7,9 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
+#include <initializer_list>
 #include <string>
 
 #include "../../include/fna2.h"
@@ -17,6 +19,7 @@
 #include "fna2_bwd.cu"
 #include "fna2_fwd.cu"
 #include "fna2_qkprep.cu"
+#include "fna2_decode.cu"
 
 namespace fna2 {
 namespace {
@@ -432,5 +435,105 @@ extern "C" int fna2_qk_prep_bwd(const Fna2QkPrepBwdArgs* b, void* stream) {
   p.dkw = a->q_weight ? b->dk_weight : nullptr;
   if (p.T == 0 || p.hq + p.hk == 0) return FNA2_OK;
   FNA2_CUDA(launch_qk_prep(p, a->head_dim, true, static_cast<cudaStream_t>(stream)));
+  return FNA2_OK;
+}
+
+namespace {
+
+int decode_num_splits(const Fna2DecodeArgs* a, int head_blocks) {
+  if (a->num_splits > 0) return a->num_splits;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t ctas = static_cast<int64_t>(a->batch) * a->kv_heads * head_blocks;
+  const int64_t want = (4LL * sms + ctas - 1) / std::max<int64_t>(ctas, 1);  // about two waves of two CTAs per SM
+  const int64_t cap = std::max<int64_t>(1, (a->capacity + 255) / 256);     // at least 256 keys per split
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({want, cap, 64})));
+}
+
+int decode_params(const Fna2DecodeArgs* a, DecodeParams* p, int* D_out, size_t* smem) {
+  FNA2_CHECK(a != nullptr, "null arguments");
+  FNA2_CHECK(a->head_dim == 64 || a->head_dim == 128, "head_dim must be 64 or 128 (got %d)", a->head_dim);
+  FNA2_CHECK(a->batch >= 0 && a->heads >= 0 && a->kv_heads > 0 && a->capacity >= 0, "bad sizes");
+  FNA2_CHECK(a->heads % a->kv_heads == 0, "heads (%d) must be a multiple of kv_heads (%d)", a->heads, a->kv_heads);
+  FNA2_CHECK(a->graph_heads >= 0 && a->graph_heads <= a->heads, "graph_heads must be in [0, heads]");
+  if (a->graph_heads > 0) {
+    FNA2_CHECK(a->rank == 16 || a->rank == 32, "rank must be 16 or 32 (got %d)", a->rank);
+    FNA2_CHECK(a->r_q && a->rk_cache && a->graph_scale, "graph heads need r_q, rk_cache and graph_scale");
+  }
+  FNA2_CHECK(a->softmax_scale > 0.f, "softmax_scale must be positive");
+  FNA2_CHECK(a->q && a->k_cache && a->v_cache && a->out && a->cache_seqlens, "null tensor pointer");
+  const bool has_new = a->k_new != nullptr;
+  FNA2_CHECK(has_new == (a->v_new != nullptr), "k_new and v_new go together");
+  if (has_new && a->graph_heads > 0) FNA2_CHECK(a->rk_new != nullptr, "k_new with graph heads needs rk_new");
+  auto al = [](const void* ptr) { return reinterpret_cast<uintptr_t>(ptr) % 16 == 0; };
+  auto st8 = [](std::initializer_list<int64_t> v) {
+    for (int64_t x : v)
+      if (x < 0 || x % 8) return false;
+    return true;
+  };
+  FNA2_CHECK(al(a->q) && al(a->k_cache) && al(a->v_cache) && al(a->out) && (!a->r_q || al(a->r_q)) &&
+                 (!a->rk_cache || al(a->rk_cache)) && (!has_new || (al(a->k_new) && al(a->v_new))) &&
+                 (!a->rk_new || al(a->rk_new)),
+             "tensor base pointers must be 16-byte aligned");
+  FNA2_CHECK(st8({a->q_batch_stride, a->q_head_stride, a->k_batch_stride, a->k_token_stride, a->k_head_stride,
+                  a->v_batch_stride, a->v_token_stride, a->v_head_stride, a->out_batch_stride, a->out_head_stride,
+                  a->rq_batch_stride, a->rq_head_stride, a->rk_batch_stride, a->rk_token_stride, a->rk_head_stride,
+                  a->kn_batch_stride, a->kn_head_stride, a->vn_batch_stride, a->vn_head_stride,
+                  a->rkn_batch_stride, a->rkn_head_stride}),
+             "strides must be non-negative multiples of 8 elements");
+  DecodeParams& d = *p;
+  d = DecodeParams{};
+  d.B = a->batch, d.H = a->heads, d.HKV = a->kv_heads, d.HG = a->graph_heads, d.R = a->graph_heads ? a->rank : 16;
+  d.G = a->heads / a->kv_heads, d.capacity = a->capacity;
+  d.scale = a->softmax_scale, d.scale_log2 = a->softmax_scale * 1.4426950408889634f;
+  using bf = __nv_bfloat16;
+  d.q = static_cast<const bf*>(a->q), d.q_sb = a->q_batch_stride, d.q_sh = a->q_head_stride;
+  d.rq = static_cast<const bf*>(a->r_q), d.rq_sb = a->rq_batch_stride, d.rq_sh = a->rq_head_stride;
+  d.kc = static_cast<bf*>(a->k_cache), d.k_sb = a->k_batch_stride, d.k_st = a->k_token_stride, d.k_sh = a->k_head_stride;
+  d.vc = static_cast<bf*>(a->v_cache), d.v_sb = a->v_batch_stride, d.v_st = a->v_token_stride, d.v_sh = a->v_head_stride;
+  d.rkc = static_cast<bf*>(a->rk_cache), d.rk_sb = a->rk_batch_stride, d.rk_st = a->rk_token_stride;
+  d.rk_sh = a->rk_head_stride;
+  d.gs = a->graph_scale, d.seqlens = a->cache_seqlens, d.offsets = a->cache_offsets;
+  d.kn = static_cast<const bf*>(a->k_new), d.kn_sb = a->kn_batch_stride, d.kn_sh = a->kn_head_stride;
+  d.vn = static_cast<const bf*>(a->v_new), d.vn_sb = a->vn_batch_stride, d.vn_sh = a->vn_head_stride;
+  d.rkn = static_cast<const bf*>(a->rk_new), d.rkn_sb = a->rkn_batch_stride, d.rkn_sh = a->rkn_head_stride;
+  d.out = static_cast<bf*>(a->out), d.o_sb = a->out_batch_stride, d.o_sh = a->out_head_stride;
+  d.lse = a->lse;
+  d.head_blocks = (d.G + 15) / 16;
+  d.splits = decode_num_splits(a, d.head_blocks);
+  const int ng_max = std::min(16, std::min(d.G, d.HG));
+  d.stages = decode_stages(a->head_dim, ng_max, d.R);
+  *smem = decode_smem_bytes(a->head_dim, ng_max, d.R, d.stages);
+  *D_out = a->head_dim;
+  return FNA2_OK;
+}
+
+}  // namespace
+
+extern "C" size_t fna2_decode_workspace_size(const Fna2DecodeArgs* a) {
+  g_last_error.clear();
+  DecodeParams p;
+  int D = 0;
+  size_t smem = 0;
+  if (decode_params(a, &p, &D, &smem) != FNA2_OK) return 0;
+  return p.splits > 1 ? static_cast<size_t>(p.B) * p.H * p.splits * (D + 2) * sizeof(float) : 0;
+}
+
+extern "C" int fna2_decode(const Fna2DecodeArgs* a, void* workspace, size_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  DecodeParams p;
+  int D = 0;
+  size_t smem = 0;
+  if (int rc = decode_params(a, &p, &D, &smem)) return rc;
+  if (p.B == 0 || p.H == 0) return FNA2_OK;
+  const size_t need = p.splits > 1 ? static_cast<size_t>(p.B) * p.H * p.splits * (D + 2) * sizeof(float) : 0;
+  if (need > 0) {
+    if (workspace == nullptr || workspace_bytes < need)
+      return fail(FNA2_ERR_WORKSPACE, "decode workspace: need %zu bytes, got %zu", need, workspace_bytes);
+    FNA2_CHECK(reinterpret_cast<uintptr_t>(workspace) % 16 == 0, "workspace must be 16-byte aligned");
+    p.ws = static_cast<float*>(workspace);
+  }
+  FNA2_CUDA(launch_decode(p, D, smem, static_cast<cudaStream_t>(stream)));
   return FNA2_OK;
 }

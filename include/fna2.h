@@ -50,7 +50,7 @@
 extern "C" {
 #endif
 
-#define FNA2_ABI_VERSION 2
+#define FNA2_ABI_VERSION 3
 
 #define FNA2_OK 0
 #define FNA2_ERR_INVALID (-1)
@@ -185,6 +185,53 @@ typedef struct Fna2QkPrepBwdArgs {
 
 /* Backward of the transform: gradients of q_in, k_in and of the two weights. */
 int fna2_qk_prep_bwd(const Fna2QkPrepBwdArgs* args, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * KV-cache decode with the relational bias.  No counterpart in the reference:
+ * its decode step (attention_fna2.py:428-432, past_kv set) bypasses FNA2 and
+ * drops graph_bias because R_k is not cached.  Here R_k is cached per graph
+ * head next to K and V, and one new query token per sequence attends to keys
+ * [0, cache_seqlens[b]) of its sequence -- plus its own new key when k_new is
+ * given, which the call also writes into the caches at slot cache_seqlens[b]
+ * (the caller then advances cache_seqlens).  Logits are those of the last
+ * query row of the prefill op above (no causal mask is needed: the query
+ * sits after every key), and out/lse follow its normalisation.
+ *
+ * Layouts (element strides; column stride 1; bases and strides 16-byte
+ * aligned): q [B, H, D], r_q [B, H_G, R], out [B, H, D]; caches
+ * k/v [B, capacity, H_KV, D] and r_k [B, capacity, H_G, R] addressed as
+ * base + b*batch_stride + slot*token_stride + head*head_stride, or, when
+ * cache_offsets is set, base + (cache_offsets[b] + slot)*token_stride +
+ * head*head_stride (packed caches; batch strides ignored); k_new/v_new
+ * [B, H_KV, D], rk_new [B, H_G, R].  lse (optional) is fp32 [B, H].
+ * A sequence with cache_seqlens[b] < 0 or more keys than capacity makes the
+ * kernel record site code 601 (fna2_device_status) and write zeros.
+ * --------------------------------------------------------------------------- */
+typedef struct Fna2DecodeArgs {
+  int batch, heads, kv_heads, graph_heads, head_dim, rank;
+  int capacity;                 /* cache slots per sequence */
+  float softmax_scale;
+  const void* q;        int64_t q_batch_stride, q_head_stride;
+  const void* r_q;      int64_t rq_batch_stride, rq_head_stride;
+  void* k_cache;        int64_t k_batch_stride, k_token_stride, k_head_stride;
+  void* v_cache;        int64_t v_batch_stride, v_token_stride, v_head_stride;
+  void* rk_cache;       int64_t rk_batch_stride, rk_token_stride, rk_head_stride;
+  const float* graph_scale;     /* [H_G] */
+  const int32_t* cache_seqlens; /* [B], device */
+  const int32_t* cache_offsets; /* [B], device, or NULL */
+  const void* k_new;    int64_t kn_batch_stride, kn_head_stride;  /* or NULL (then v_new, rk_new too) */
+  const void* v_new;    int64_t vn_batch_stride, vn_head_stride;
+  const void* rk_new;   int64_t rkn_batch_stride, rkn_head_stride;
+  void* out;            int64_t out_batch_stride, out_head_stride;
+  float* lse;                   /* or NULL */
+  int num_splits;               /* key splits per (sequence, head); 0 = chosen by the library */
+} Fna2DecodeArgs;
+
+/* Bytes of fp32 workspace fna2_decode needs for these arguments (0 when the
+ * keys of a (sequence, head) are not split). */
+size_t fna2_decode_workspace_size(const Fna2DecodeArgs* args);
+
+int fna2_decode(const Fna2DecodeArgs* args, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Message of the last failed call on this host thread ("" if none). */
 const char* fna2_last_error(void);

@@ -176,3 +176,74 @@ def test_module_constants_keep_reference_contract():
     import fna2_b200
     assert fna2_b200.BLOCK_R == 32  # NaylisAttention requires rel_rank == BLOCK_R (attention_fna2.py:225)
     assert fna2_b200.BLOCK_M == 128
+
+
+def test_decode_struct_layout_matches_c(tmp_path):
+    src = tmp_path / "dec.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "fna2.h"\n'
+                   'int main(){printf("%zu %zu %zu %zu %zu\\n", sizeof(Fna2DecodeArgs),'
+                   ' offsetof(Fna2DecodeArgs, q), offsetof(Fna2DecodeArgs, cache_offsets),'
+                   ' offsetof(Fna2DecodeArgs, rk_new), offsetof(Fna2DecodeArgs, num_splits));}\n')
+    exe = tmp_path / "dec"
+    subprocess.check_call(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)])
+    got = [int(x) for x in subprocess.check_output([str(exe)]).split()]
+    D = _lib.Fna2DecodeArgs
+    assert got == [ctypes.sizeof(D), D.q.offset, D.cache_offsets.offset, D.rk_new.offset, D.num_splits.offset]
+
+
+def _dec_args(**over):
+    a = _lib.Fna2DecodeArgs()
+    a.batch, a.heads, a.kv_heads, a.graph_heads, a.head_dim, a.rank = 2, 4, 2, 4, 128, 16
+    a.capacity, a.softmax_scale = 64, 0.088
+    buf = ctypes.create_string_buffer(1 << 16)
+    base = (ctypes.addressof(buf) + 255) // 256 * 256
+    for name in ("q", "r_q", "k_cache", "v_cache", "rk_cache", "graph_scale", "cache_seqlens", "out"):
+        setattr(a, name, base)
+    a.q_batch_stride, a.q_head_stride = 512, 128
+    a.k_batch_stride, a.k_token_stride, a.k_head_stride = 64 * 256, 256, 128
+    a.v_batch_stride, a.v_token_stride, a.v_head_stride = 64 * 256, 256, 128
+    a.rk_batch_stride, a.rk_token_stride, a.rk_head_stride = 64 * 64, 64, 16
+    a.rq_batch_stride, a.rq_head_stride = 64, 16
+    a.out_batch_stride, a.out_head_stride = 512, 128
+    for k, v in over.items():
+        setattr(a, k, v)
+    return a, buf
+
+
+@pytest.mark.parametrize("field,value,msg", [
+    ("head_dim", 96, "head_dim"),
+    ("kv_heads", 3, "multiple of kv_heads"),
+    ("rank", 24, "rank"),
+    ("graph_heads", 5, "graph_heads"),
+    ("q_head_stride", 100, "strides"),
+    ("softmax_scale", 0.0, "softmax_scale"),
+])
+def test_decode_invalid_arguments_rejected(field, value, msg):
+    lib = _lib.load()
+    a, _buf = _dec_args(**{field: value})
+    assert lib.fna2_decode(a, None, 0, None) == _lib.FNA2_ERR_INVALID
+    assert msg in lib.fna2_last_error().decode()
+
+
+def test_decode_pairs_and_alignment_checked():
+    lib = _lib.load()
+    a, buf = _dec_args()
+    a.k_new = a.q  # without v_new
+    assert lib.fna2_decode(a, None, 0, None) == _lib.FNA2_ERR_INVALID
+    assert "k_new and v_new" in lib.fna2_last_error().decode()
+    a, buf = _dec_args()
+    a.k_cache = a.k_cache + 8
+    assert lib.fna2_decode(a, None, 0, None) == _lib.FNA2_ERR_INVALID
+    assert "aligned" in lib.fna2_last_error().decode()
+
+
+def test_decode_workspace_size_and_empty_batch():
+    lib = _lib.load()
+    a, _buf = _dec_args(num_splits=4)
+    assert lib.fna2_decode_workspace_size(a) == 2 * 4 * 4 * (128 + 2) * 4
+    a, _buf = _dec_args(num_splits=1)
+    assert lib.fna2_decode_workspace_size(a) == 0
+    a, _buf = _dec_args(num_splits=4)
+    assert lib.fna2_decode(a, None, 0, None) == _lib.FNA2_ERR_WORKSPACE
+    a, _buf = _dec_args(batch=0)
+    assert lib.fna2_decode(a, None, 0, None) == _lib.FNA2_OK
