@@ -192,34 +192,66 @@ __global__ void __launch_bounds__(kDecThreads) fna2_decode_kernel(const DecodePa
   const int kpieces = L.ke / 8, vpieces = D / 8;  // 16-byte pieces per row
   const int64_t kbase_b = p.offsets ? 0 : b * p.k_sb, vbase_b = p.offsets ? 0 : b * p.v_sb;
   const int64_t rbase_b = p.offsets ? 0 : b * p.rk_sb;
+  // Whole tiles away from the appended slot take a fast path: each lane copies
+  // fixed 16-byte pieces (column c of rows r0, r0 + RPP, ...) of K and V and
+  // steps one pointer per pass; the tile holding the new token, and a partial
+  // last tile, take the general path.
+  constexpr int PPR = D / 8, RPP = 32 / PPR;  // pieces per K/V row, rows per pass
+  const int pc = lane % PPR, pr0 = lane / PPR;
+  const int rpieces = kpieces - PPR;          // R_k pieces per row (ng * R / 8)
+  const int64_t kstep = static_cast<int64_t>(RPP) * p.k_st, vstep = static_cast<int64_t>(RPP) * p.v_st;
+  const __nv_bfloat16* kcol = p.kc + kbase_b + seq_row * p.k_st + kh * p.k_sh + pc * 8;
+  const __nv_bfloat16* vcol = p.vc + vbase_b + seq_row * p.v_st + kh * p.v_sh + pc * 8;
   int issued = 0;
+  auto issue_general = [&](uint8_t* st, int j0) {
+    for (int e = lane; e < kDecKeys * (kpieces + vpieces); e += 32) {
+      const bool is_v = e >= kDecKeys * kpieces;
+      const int ee = is_v ? e - kDecKeys * kpieces : e;
+      const int np = is_v ? vpieces : kpieces;
+      const int r = ee / np, c = ee % np, j = j0 + r;
+      const bool valid = j < k_end;
+      const bool fresh = has_new && j == len0;
+      const int64_t row = seq_row + j;
+      const __nv_bfloat16* src;
+      if (is_v) {
+        src = fresh ? p.vn + b * p.vn_sb + kh * p.vn_sh : p.vc + vbase_b + row * p.v_st + kh * p.v_sh;
+        src += c * 8;
+      } else if (c < D / 8) {
+        src = fresh ? p.kn + b * p.kn_sb + kh * p.kn_sh : p.kc + kbase_b + row * p.k_st + kh * p.k_sh;
+        src += c * 8;
+      } else {
+        const int g = (c - D / 8) / (p.R / 8), rc = (c - D / 8) % (p.R / 8);
+        src = fresh ? p.rkn + b * p.rkn_sb + (h0 + g) * p.rkn_sh
+                    : p.rkc + rbase_b + row * p.rk_st + (h0 + g) * p.rk_sh;
+        src += rc * 8;
+      }
+      uint8_t* dst = is_v ? st + kDecKeys * L.k_stride + r * L.v_stride + c * 16 : st + r * L.k_stride + c * 16;
+      dec_cp16(dst, valid ? static_cast<const void*>(src) : static_cast<const void*>(p.q), valid);
+    }
+  };
   auto issue = [&]() {
     if (issued < n_tiles) {
       uint8_t* st = ring + (issued % p.stages) * L.stage;
       const int j0 = k_begin + (warp + issued * kDecWarps) * kDecKeys;
-      for (int e = lane; e < kDecKeys * (kpieces + vpieces); e += 32) {
-        const bool is_v = e >= kDecKeys * kpieces;
-        const int ee = is_v ? e - kDecKeys * kpieces : e;
-        const int np = is_v ? vpieces : kpieces;
-        const int r = ee / np, c = ee % np, j = j0 + r;
-        const bool valid = j < k_end;
-        const bool fresh = has_new && j == len0;
-        const int64_t row = seq_row + j;
-        const __nv_bfloat16* src;
-        if (is_v) {
-          src = fresh ? p.vn + b * p.vn_sb + kh * p.vn_sh : p.vc + vbase_b + row * p.v_st + kh * p.v_sh;
-          src += c * 8;
-        } else if (c < D / 8) {
-          src = fresh ? p.kn + b * p.kn_sb + kh * p.kn_sh : p.kc + kbase_b + row * p.k_st + kh * p.k_sh;
-          src += c * 8;
-        } else {
-          const int g = (c - D / 8) / (p.R / 8), rc = (c - D / 8) % (p.R / 8);
-          src = fresh ? p.rkn + b * p.rkn_sb + (h0 + g) * p.rkn_sh
-                      : p.rkc + rbase_b + row * p.rk_st + (h0 + g) * p.rk_sh;
-          src += rc * 8;
+      const bool whole = j0 + kDecKeys <= k_end && !(has_new && len0 >= j0 && len0 < j0 + kDecKeys);
+      if (!whole) {
+        issue_general(st, j0);
+      } else {
+        const __nv_bfloat16* ks = kcol + static_cast<int64_t>(j0 + pr0) * p.k_st;
+        const __nv_bfloat16* vs = vcol + static_cast<int64_t>(j0 + pr0) * p.v_st;
+        uint8_t* kd = st + pr0 * L.k_stride + pc * 16;
+        uint8_t* vd = st + kDecKeys * L.k_stride + pr0 * L.v_stride + pc * 16;
+#pragma unroll
+        for (int i = 0; i < kDecKeys / RPP; ++i) {
+          dec_cp16(kd + i * RPP * L.k_stride, ks + i * kstep, true);
+          dec_cp16(vd + i * RPP * L.v_stride, vs + i * vstep, true);
         }
-        uint8_t* dst = is_v ? st + kDecKeys * L.k_stride + r * L.v_stride + c * 16 : st + r * L.k_stride + c * 16;
-        dec_cp16(dst, valid ? static_cast<const void*>(src) : static_cast<const void*>(p.q), valid);
+        for (int e = lane; e < kDecKeys * rpieces; e += 32) {  // R_k of the block's graph heads
+          const int r = e / rpieces, c = e % rpieces;
+          const int gh = c / (p.R / 8), rc = c % (p.R / 8);
+          const __nv_bfloat16* src = p.rkc + rbase_b + (seq_row + j0 + r) * p.rk_st + (h0 + gh) * p.rk_sh + rc * 8;
+          dec_cp16(st + r * L.k_stride + (PPR + c) * 16, src, true);
+        }
       }
     }
     ++issued;
@@ -270,8 +302,10 @@ __global__ void __launch_bounds__(kDecThreads) fna2_decode_kernel(const DecodePa
     l0 = l0 * c0 + (x[0] + x[1] + x[2] + x[3]);
     l1 = l1 * c1 + (x[4] + x[5] + x[6] + x[7]);
     m0 = n0, m1 = n1;
+    if (__any_sync(0xffffffffu, c0 != 1.f || c1 != 1.f)) {  // no row max moved: the factors are exactly 1
 #pragma unroll
-    for (int i = 0; i < D / 8; ++i) acc[i][0] *= c0, acc[i][1] *= c0, acc[i][2] *= c1, acc[i][3] *= c1;
+      for (int i = 0; i < D / 8; ++i) acc[i][0] *= c0, acc[i][1] *= c0, acc[i][2] *= c1, acc[i][3] *= c1;
+    }
     // O += P V: P (16 heads x 16 keys) is the A operand straight from the S fragments
     const uint32_t pa[4] = {pack_bf16(x[0], x[1]), pack_bf16(x[4], x[5]), pack_bf16(x[2], x[3]),
                             pack_bf16(x[6], x[7])};
