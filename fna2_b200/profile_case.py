@@ -12,6 +12,12 @@ repetition's launches (e.g. ``ncu -k regex:fna2_... -s 3 -c 3``).
 runs the varlen QK-RMSNorm + RoPE transform instead: ``batch`` packed sequences of
 ``seqlen`` tokens, ``heads`` query and key heads (bf16), bf16 norm weights, RoPE
 on; each repetition launches its forward and its backward kernel once.
+
+    python -m fna2_b200.profile_case --op decode --batch 32 --heads 32 --seqlen 4096 --head-dim 128 --rank 16 --reps 2
+
+runs one KV-cache decode step per repetition: ``batch`` sequences with
+``seqlen`` cached keys each (dense caches, H_KV = heads, all graph heads), one
+new token per sequence appended and attended.
 """
 import argparse
 import math
@@ -29,10 +35,12 @@ def main(argv=None):
     ap.add_argument("--head-dim", type=int, default=128)
     ap.add_argument("--rank", type=int, default=16)
     ap.add_argument("--reps", type=int, default=2)
-    ap.add_argument("--op", default="attention", choices=["attention", "qk_prep"])
+    ap.add_argument("--op", default="attention", choices=["attention", "qk_prep", "decode"])
     a = ap.parse_args(argv)
     if a.op == "qk_prep":
         return qk_prep_case(a)
+    if a.op == "decode":
+        return decode_case(a)
     g = torch.Generator(device="cuda").manual_seed(0)
     shape = (a.batch, a.heads, a.seqlen, a.head_dim)
     q, k, v, do = (torch.randn(shape, device="cuda", generator=g).bfloat16() for _ in range(4))
@@ -65,6 +73,23 @@ def qk_prep_case(a):
     for _ in range(a.reps):
         qo, ko = apply_qk_norm_rope_varlen(q, k, cu, norms[0], norms[1], rope)
         torch.autograd.backward((qo, ko), (dq_out, dk_out))
+    torch.cuda.synchronize()
+    print("ok")
+
+
+def decode_case(a):
+    from .decode import flash_naylis_decode
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    B, H, D, R, L = a.batch, a.heads, a.head_dim, a.rank, a.seqlen
+    kc, vc = (torch.randn(B, L + 1, H, D, device="cuda", generator=g).bfloat16() for _ in range(2))
+    rkc = (torch.randn(B, L + 1, H, R, device="cuda", generator=g) * 0.25).bfloat16()
+    q, kn, vn = (torch.randn(B, H, D, device="cuda", generator=g).bfloat16() for _ in range(3))
+    rq, rkn = ((torch.randn(B, H, R, device="cuda", generator=g) * 0.25).bfloat16() for _ in range(2))
+    gs = torch.ones(H, device="cuda")
+    seq = torch.full((B,), L, dtype=torch.int32, device="cuda")
+    for _ in range(a.reps):
+        flash_naylis_decode(q, kc, vc, seq, rq, rkc, gs, kn, vn, rkn)
     torch.cuda.synchronize()
     print("ok")
 
