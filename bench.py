@@ -28,6 +28,11 @@ sequence's cache holds its L tokens (packed caches, K/V/R_k), one new token
 per sequence is appended and attends to L + 1 keys; HBM GB/s of the step
 against the measured copy bandwidth, with the decode oracle
 (oracle/decode_oracle.py) timed on the host beside it.
+
+``--op rel_proj`` measures the fused R_q/R_k projection (fna2_b200/rel_proj.py:
+one cuBLAS GEMM over the stacked weights, strided views out) forward + backward
+on the workload's tokens (x [T, H*D] bf16), with the reference's two-Linear
+composition timed on the same GPU beside it.
 """
 from __future__ import annotations
 
@@ -536,6 +541,72 @@ def run_decode(args, w):
     }))
 
 
+def run_rel_proj(args, w):
+    """Fused R_q/R_k projection (one GEMM over the stacked weights) fwd + bwd, one GPU."""
+    import torch.nn.functional as F
+    from fna2_b200.rel_proj import compute_rq_rk
+    dev = "cuda"
+    lengths, H, D, R = w["lengths"], w["H"], w["D"], w["r"]
+    T, E, n = sum(lengths), H * D, H * R
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(T, E, device=dev, generator=g, dtype=torch.bfloat16).requires_grad_(True)
+    wq = (torch.randn(n, E, device=dev, generator=g) * 0.01).bfloat16().requires_grad_(True)
+    wk = (torch.randn(n, E, device=dev, generator=g) * 0.01).bfloat16().requires_grad_(True)
+    w_st = torch.cat([wq.detach(), wk.detach()]).requires_grad_(True)
+    gq = torch.randn(T, H, R, device=dev, generator=g, dtype=torch.bfloat16)
+    gk = torch.randn(T, H, R, device=dev, generator=g, dtype=torch.bfloat16)
+
+    def fused():
+        x.grad = w_st.grad = None
+        rq, rk = compute_rq_rk(x, w_st, H, R)
+        torch.autograd.backward([rq, rk], [gq, gk])
+
+    def reference():  # attention_fna2.py:332-333: two Linear layers, view, cast, contiguous
+        x.grad = wq.grad = wk.grad = None
+        rq = F.linear(x, wq).view(T, H, R).to(torch.bfloat16).contiguous()
+        rk = F.linear(x, wk).view(T, H, R).to(torch.bfloat16).contiguous()
+        torch.autograd.backward([rq, rk], [gq, gk])
+
+    def timeit(fn):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        t0.record()
+        for _ in range(args.steps):
+            fn()
+        t1.record()
+        torch.cuda.synchronize()
+        return t0.elapsed_time(t1) / args.steps
+
+    clocks = ClockSampler(0)
+    clocks.start()
+    ms = timeit(fused)
+    clk = clocks.stop()
+    ms_ref = timeit(reference)
+    flops = 6.0 * T * E * 2 * n  # forward, dX and dW GEMMs over N = 2 * H_G * R
+    tf = flops / (ms / 1e3) / 1e12
+    peak, peak_src = None, "measured"
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = json.load(f).get("bf16_tflops")
+    except Exception:
+        pass
+    if peak is None:
+        peak, peak_src = 1590.0, "fallback"
+    print(json.dumps({
+        "metric": "R_q/R_k projection fwd+bwd TFLOP/s (bf16, one GEMM over the stacked weights)",
+        "value": tf, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": w["desc"] + f"; x [T, {E}] bf16, H_G = {H}, R = {R}", "tokens": T,
+                   "reference_two_linears_ms": ms_ref, "speedup_vs_reference_composition": ms_ref / ms,
+                   "gemm": "cuBLAS via torch (plain library GEMM)"},
+        "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
+                     "peak_source": peak_src},
+        "clocks": clk,
+    }))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -546,13 +617,15 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
-    ap.add_argument("--op", default="attention", choices=["attention", "qk_prep", "decode"])
+    ap.add_argument("--op", default="attention", choices=["attention", "qk_prep", "decode", "rel_proj"])
     args = ap.parse_args()
     w = workload(args.workload)
     if args.op == "qk_prep":
         run_qk_prep(args, w)
     elif args.op == "decode":
         run_decode(args, w)
+    elif args.op == "rel_proj":
+        run_rel_proj(args, w)
     elif args.impl == "reference":
         run_reference(args, w)
     else:
