@@ -513,15 +513,14 @@ def run_decode(args, w):
     if not args.no_cpu:
         torch.set_num_threads(os.cpu_count())
         sample = [b for b in range(B) if lengths[b] <= 2048][:8]
-        cb = 0
         qs, rqs = q[sample].cpu(), rq[sample].cpu()
         kcs = [kc[offs[b]:offs[b] + lengths[b]].cpu() for b in sample]
         vcs = [vc[offs[b]:offs[b] + lengths[b]].cpu() for b in sample]
         rks = [rkc[offs[b]:offs[b] + lengths[b]].cpu() for b in sample]
         Lm = max(lengths[b] for b in sample)
-        pad = lambda ts, x: torch.stack([torch.nn.functional.pad(t, (0, 0, 0, 0, 0, Lm - t.shape[0])) for t in ts])
+        pad = lambda ts: torch.stack([torch.nn.functional.pad(t, (0, 0, 0, 0, 0, Lm - t.shape[0])) for t in ts])
         t_c = time.perf_counter()
-        DO.decode(qs, pad(kcs, 0), pad(vcs, 0), [lengths[b] for b in sample], rqs, pad(rks, 0), gs.cpu(),
+        DO.decode(qs, pad(kcs), pad(vcs), [lengths[b] for b in sample], rqs, pad(rks), gs.cpu(),
                   kn[sample].cpu(), vn[sample].cpu(), rkn[sample].cpu())
         dt = time.perf_counter() - t_c
         cb = sum(lengths[b] for b in sample) * (2 * H_KV * D + H * R) * 2
