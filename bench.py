@@ -11,7 +11,9 @@ One step = forward + backward of every sequence a rank owns.  ``value`` is
 total algorithmic FLOPs of the whole batch / max-over-ranks step time (device
 resident inputs); ``e2e`` is the same metric through the public API
 (``flash_naylis_attn`` + ``backward``) with the step's inputs copied from
-pinned host memory and d_graph_scale read back every step.
+pinned host memory and d_graph_scale read back every step; the sequences go
+through in 8 groups so that one group's host-to-device copy (PCIe) overlaps
+the previous group's compute.
 
 ``--impl reference`` times the reference's eager path restated on the CPU
 (oracle/fna2_oracle.py: materialised bias + SDPA + autograd, fp32, all host
@@ -311,17 +313,52 @@ def run_gpu(args, w):
         dev_do = do
         gsl = gs.clone().requires_grad_(True)
         res_host = torch.empty(H, dtype=torch.float32).pin_memory()
+        # Sequences go through in G contiguous groups of about T/G tokens: the inputs of
+        # group g+1 cross PCIe on a copy stream while group g computes (each group's
+        # buffers are written again only after that group's compute of the previous step).
+        G = 8
+        bounds, acc_t = [0], 0
+        for i, L in enumerate(mine):
+            acc_t += L
+            if acc_t >= T * len(bounds) / G and len(bounds) < G:
+                bounds.append(i + 1)
+        if bounds[-1] != len(mine):
+            bounds.append(len(mine))
+        groups = []
+        for a, b in zip(bounds[:-1], bounds[1:]):
+            t0g, t1g = cu[a], cu[b]
+            cu_g = torch.tensor([c - t0g for c in cu[a:b + 1]], dtype=torch.int32, device=dev)
+            groups.append((t0g, t1g, cu_g, max(mine[a:b])))
+        copy_stream = torch.cuda.Stream(device=dev)
+        done = [torch.cuda.Event() for _ in groups]
+        for e in done:
+            e.record(stream)
 
         def e2e_step():
-            for dst, src in zip(leaves + [dev_do], host):
-                dst.copy_(src, non_blocking=True)
-            ins = [t.detach().requires_grad_(True) for t in leaves]
+            start = torch.cuda.Event()
+            start.record(stream)
+            copied = []
+            with torch.cuda.stream(copy_stream):
+                copy_stream.wait_event(start)
+                for gi, (t0g, t1g, _, _) in enumerate(groups):
+                    copy_stream.wait_event(done[gi])
+                    for dst, src in zip(leaves + [dev_do], host):
+                        dst[t0g:t1g].copy_(src[t0g:t1g], non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(copy_stream)
+                    copied.append(ev)
             gsl.grad = None
-            out = flash_naylis_attn(*ins, gsl, softmax_scale=scale, is_causal=True, cu_seqlens_q=cu_t,
-                                    cu_seqlens_k=cu_t, max_seqlen_q=msl, max_seqlen_k=msl)
-            out.backward(dev_do)
+            keep = []
+            for gi, (t0g, t1g, cu_g, msl_g) in enumerate(groups):
+                stream.wait_event(copied[gi])
+                ins = [t[t0g:t1g].detach().requires_grad_(True) for t in leaves]
+                out = flash_naylis_attn(*ins, gsl, softmax_scale=scale, is_causal=True, cu_seqlens_q=cu_g,
+                                        cu_seqlens_k=cu_g, max_seqlen_q=msl_g, max_seqlen_k=msl_g)
+                out.backward(dev_do[t0g:t1g])
+                done[gi].record(stream)
+                keep.append((ins, out))
             res_host.copy_(gsl.grad, non_blocking=True)
-            return ins, out
+            return keep
 
         for _ in range(W):
             e2e_step()
