@@ -63,27 +63,54 @@ __global__ void __launch_bounds__(128) fna2_bwd_pre_kernel(const BwdParams p) {
   const int row = blockIdx.x * 128 + threadIdx.x;
   if (blockIdx.x == 0 && h == 0 && bz == 0 && p.dgs != nullptr && static_cast<int>(threadIdx.x) < P.heads_graph)
     p.dgs[threadIdx.x] = 0.f;
-  if (row < p.total_q_rows) {
-    const __nv_bfloat16* o = p.out + bz * p.o_sb + h * p.o_sh + static_cast<int64_t>(row) * p.o_sr;
-    const __nv_bfloat16* g = p.dout + bz * p.do_sb + h * p.do_sh + static_cast<int64_t>(row) * p.do_sr;
-    float acc = 0.f;
+  {
+    // Delta = rowsum(dO * O): a row is read by D/8 lanes (16 bytes each), so every
+    // load instruction covers whole rows; each warp owns 32 of the block's rows.
+    constexpr int LPR = D / 8, RPI = 32 / LPR, ITERS = 32 / RPI, BATCH = ITERS < 8 ? ITERS : 8;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sub = lane % LPR, rsel = lane / LPR;
+    const int row_base = blockIdx.x * 128 + warp * 32;
+    const int64_t sbh = static_cast<int64_t>(bz) * P.heads + h;
 #pragma unroll
-    for (int c = 0; c < D; c += 8) {
-      const uint4 a = *reinterpret_cast<const uint4*>(o + c);
-      const uint4 b = *reinterpret_cast<const uint4*>(g + c);
-      const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
-      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&b);
+    for (int i0 = 0; i0 < ITERS; i0 += BATCH) {
+      uint4 a[BATCH], b[BATCH];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 x = __bfloat1622float2(a2[i]);
-        const float2 y = __bfloat1622float2(b2[i]);
-        acc = fmaf(x.x, y.x, acc);
-        acc = fmaf(x.y, y.y, acc);
+      for (int i = 0; i < BATCH; ++i) {
+        const int r = row_base + (i0 + i) * RPI + rsel;
+        a[i] = b[i] = make_uint4(0u, 0u, 0u, 0u);
+        if (r < p.total_q_rows) {
+          a[i] = *reinterpret_cast<const uint4*>(p.out + bz * p.o_sb + h * p.o_sh + static_cast<int64_t>(r) * p.o_sr +
+                                                 sub * 8);
+          b[i] = *reinterpret_cast<const uint4*>(p.dout + bz * p.do_sb + h * p.do_sh +
+                                                 static_cast<int64_t>(r) * p.do_sr + sub * 8);
+        }
+      }
+      float acc[BATCH];
+#pragma unroll
+      for (int i = 0; i < BATCH; ++i) {
+        const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a[i]);
+        const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&b[i]);
+        acc[i] = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 x = __bfloat1622float2(a2[k]);
+          const float2 y = __bfloat1622float2(b2[k]);
+          acc[i] = fmaf(x.x, y.x, acc[i]);
+          acc[i] = fmaf(x.y, y.y, acc[i]);
+        }
+      }
+#pragma unroll
+      for (int o = LPR / 2; o > 0; o >>= 1)
+#pragma unroll
+        for (int i = 0; i < BATCH; ++i) acc[i] += __shfl_xor_sync(0xffffffffu, acc[i], o);
+#pragma unroll
+      for (int i = 0; i < BATCH; ++i) {
+        const int r = row_base + (i0 + i) * RPI + rsel;
+        if (sub == 0 && r < p.total_q_rows) {
+          p.ws_delta[sbh * p.ws_sbh + r] = acc[i];
+          p.ws_lse2[sbh * p.ws_sbh + r] = p.lse[sbh * p.lse_sbh + r] * kLog2e;
+        }
       }
     }
-    const int64_t idx = (static_cast<int64_t>(bz) * P.heads + h) * p.ws_sbh + row;
-    p.ws_delta[idx] = acc;
-    p.ws_lse2[idx] = p.lse[(static_cast<int64_t>(bz) * P.heads + h) * p.lse_sbh + row] * kLog2e;
   }
   if (P.varlen) {
     // rows outside [cu[0], cu[N]) are not owned by any tile: zero them
