@@ -1,7 +1,7 @@
 """Generate the golden fixtures under ``tests/golden/`` from the REFERENCE itself.
 
 Run in a container that has the reference source mounted (it is imported from
-``$FNA2_REFERENCE``, default ``/root/reference/FNA2``); the fixtures it writes
+``$FNA2_REFERENCE``, default: the mounted reference checkout's FNA2 directory); the fixtures it writes
 are committed, so nothing else ever needs the reference at run time.
 
 Two witnesses of the reference are recorded:
