@@ -142,3 +142,21 @@ def test_bad_length_sets_status_and_writes_zeros():
     assert lib.fna2_device_status(1) == 601
     assert (out[1] == 0).all()
     assert lib.fna2_device_status(0) == 0
+
+
+def test_reference_cache_layout_and_largest_head_block():
+    """Caches in the reference's [B, H_KV, S, D] layout passed as .transpose(1, 2),
+    16 graph heads per KV head at rank 32 (the largest shared-memory layout)."""
+    from fna2_b200.decode import flash_naylis_decode
+    lens, H, H_KV, D, R = [5, 300, 64], 32, 2, 128, 32
+    cap = 320
+    q, kc, vc, rq, rkc, gs, new = _inputs(lens, H, H_KV, H, D, R, cap, 23, True)
+    k_ref = kc.transpose(1, 2).contiguous().cuda()  # [B, H_KV, S, D] storage
+    v_ref = vc.transpose(1, 2).contiguous().cuda()
+    seq = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    out = flash_naylis_decode(q.cuda(), k_ref.transpose(1, 2), v_ref.transpose(1, 2), seq, rq.cuda(), rkc.cuda(),
+                              gs.cuda(), k=new[0].cuda(), v=new[1].cuda(), r_k=new[2].cuda())
+    ro, _ = DO.decode(q, kc, vc, lens, rq, rkc, gs, k_new=new[0], v_new=new[1], rk_new=new[2])
+    _close("out", out, ro)
+    for b, n in enumerate(lens):
+        assert torch.equal(k_ref[b, :, n].cpu(), new[0][b])
