@@ -258,7 +258,7 @@ extern "C" size_t fna2_bwd_workspace_size(const Fna2Problem* prob) {
   if (!prob) return 0;
   Shape s;
   if (check_problem(*prob, &s)) return 0;
-  return bwd_workspace_bytes(s.batch_dim(), s.H, s.HG, s.rows_q());
+  return bwd_workspace_bytes(s.batch_dim(), s.H, s.HG, s.rows_q(), s.varlen, s.rows_k(), s.B);
 }
 
 extern "C" int fna2_bwd(const Fna2BwdArgs* a, void* stream) {
@@ -279,7 +279,7 @@ extern "C" int fna2_bwd(const Fna2BwdArgs* a, void* stream) {
     if (int rc = check_tensor(a->dr_k, "dr_k", s.varlen)) return rc;
     FNA2_CHECK(a->graph_scale != nullptr && a->d_graph_scale != nullptr, "graph_scale/d_graph_scale: null");
   }
-  const size_t need = bwd_workspace_bytes(s.batch_dim(), s.H, s.HG, s.rows_q());
+  const size_t need = bwd_workspace_bytes(s.batch_dim(), s.H, s.HG, s.rows_q(), s.varlen, s.rows_k(), s.B);
   if (a->workspace_bytes < need || (need && a->workspace == nullptr))
     return fail(FNA2_ERR_WORKSPACE, "workspace too small: %zu < %zu bytes", a->workspace_bytes, need);
   FNA2_CHECK((reinterpret_cast<uintptr_t>(a->workspace) & 255u) == 0, "workspace must be 256-byte aligned");
@@ -342,7 +342,7 @@ extern "C" int fna2_bwd(const Fna2BwdArgs* a, void* stream) {
   p.batch = s.B;
   p.n_mblocks = (s.Sq + kBlockM - 1) / kBlockM;
   p.n_nblocks = (s.Sk + kBlockN - 1) / kBlockN;
-  bwd_set_workspace(&p, a->workspace, s.batch_dim(), s.H, s.rows_q());
+  bwd_set_workspace(&p, a->workspace, s.batch_dim(), s.H, s.rows_q(), s.varlen, s.rows_k(), s.B);
   FNA2_CUDA(launch_bwd(s.D, s.RP, m, p, static_cast<cudaStream_t>(stream),
                        reinterpret_cast<cudaEvent_t*>(a->launch_events)));
   return FNA2_OK;

@@ -35,16 +35,35 @@ namespace fna2 {
 
 inline size_t bwd_ws_align(size_t x) { return (x + 255) & ~size_t(255); }
 
-inline size_t bwd_workspace_bytes(int batch_dim, int H, int /*HG*/, int rows) {
+// Varlen tile tables: at most ceil(T/128) + N real tiles per kind (query tiles for
+// the dQ kernel, key tiles for the dK/dV kernel), 32 bytes per entry.
+inline int bwd_tab_len(int rows, int n_seqs) { return (rows + kBlockM - 1) / kBlockM + n_seqs; }
+
+// Workspace: log2-domain LSE and Delta (fp32 per query row and head), then, for
+// varlen problems, the two tile tables.
+inline size_t bwd_workspace_bytes(int batch_dim, int H, int /*HG*/, int rows, bool varlen = false, int rows_k = 0,
+                                  int n_seqs = 0) {
   const size_t n = static_cast<size_t>(batch_dim) * H * rows;
-  return 2 * bwd_ws_align(n * sizeof(float));
+  size_t bytes = 2 * bwd_ws_align(n * sizeof(float));
+  if (varlen)
+    bytes += bwd_ws_align((static_cast<size_t>(bwd_tab_len(rows, n_seqs)) + bwd_tab_len(rows_k, n_seqs)) * 32);
+  return bytes;
 }
 
-inline void bwd_set_workspace(BwdParams* p, void* ws, int batch_dim, int H, int rows) {
+inline void bwd_set_workspace(BwdParams* p, void* ws, int batch_dim, int H, int rows, bool varlen = false,
+                              int rows_k = 0, int n_seqs = 0) {
   const size_t n = static_cast<size_t>(batch_dim) * H * rows;
   p->ws_lse2 = static_cast<float*>(ws);
   p->ws_delta = reinterpret_cast<float*>(static_cast<char*>(ws) + bwd_ws_align(n * sizeof(float)));
   p->ws_sbh = rows;
+  p->tab_q = p->tab_k = nullptr;
+  p->tab_q_len = p->tab_k_len = 0;
+  if (varlen) {
+    p->tab_q_len = bwd_tab_len(rows, n_seqs);
+    p->tab_k_len = bwd_tab_len(rows_k, n_seqs);
+    p->tab_q = reinterpret_cast<int4*>(static_cast<char*>(ws) + 2 * bwd_ws_align(n * sizeof(float)));
+    p->tab_k = p->tab_q + 2 * static_cast<size_t>(p->tab_q_len);
+  }
 }
 
 __device__ __forceinline__ void zero_row(__nv_bfloat16* row, int n) {
@@ -63,6 +82,47 @@ __global__ void __launch_bounds__(128) fna2_bwd_pre_kernel(const BwdParams p) {
   const int row = blockIdx.x * 128 + threadIdx.x;
   if (blockIdx.x == 0 && h == 0 && bz == 0 && p.dgs != nullptr && static_cast<int>(threadIdx.x) < P.heads_graph)
     p.dgs[threadIdx.x] = 0.f;
+  if (blockIdx.x == 0 && h == 0 && bz == 0 && P.varlen) {
+    // tile tables of the varlen kernels: per sequence (in order) its query tiles, heaviest
+    // causal tile first, and its key tiles; the unused tail is marked with tile = -1
+    __shared__ int scan_s[2][4];
+    int carry_q = 0, carry_k = 0;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    for (int base = 0; base < p.batch; base += 128) {
+      const int z = base + static_cast<int>(threadIdx.x);
+      int qs = 0, ks = 0, lq = 0, lk = 0;
+      if (z < p.batch) {
+        qs = __ldg(P.cu_q + z), lq = __ldg(P.cu_q + z + 1) - qs;
+        ks = __ldg(P.cu_k + z), lk = __ldg(P.cu_k + z + 1) - ks;
+      }
+      const int tq = (lq + kBlockM - 1) / kBlockM, tk = (lk + kBlockN - 1) / kBlockN;
+      int iq = tq, ik = tk;  // inclusive scans within the warp
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int uq = __shfl_up_sync(0xffffffffu, iq, o), uk = __shfl_up_sync(0xffffffffu, ik, o);
+        if (lane >= o) iq += uq, ik += uk;
+      }
+      if (lane == 31) scan_s[0][w] = iq, scan_s[1][w] = ik;
+      __syncthreads();
+      int oq = carry_q + iq - tq, ok = carry_k + ik - tk;
+      for (int i = 0; i < w; ++i) oq += scan_s[0][i], ok += scan_s[1][i];
+      for (int t = 0; t < tq && oq + t < p.tab_q_len; ++t) {  // (bounded even for inconsistent cu_seqlens)
+        p.tab_q[2 * (oq + t)] = make_int4(tq - 1 - t, qs, ks, lq);
+        p.tab_q[2 * (oq + t) + 1] = make_int4(lk, z, 0, 0);
+      }
+      for (int t = 0; t < tk && ok + t < p.tab_k_len; ++t) {
+        p.tab_k[2 * (ok + t)] = make_int4(t, qs, ks, lq);
+        p.tab_k[2 * (ok + t) + 1] = make_int4(lk, z, 0, 0);
+      }
+      carry_q += scan_s[0][0] + scan_s[0][1] + scan_s[0][2] + scan_s[0][3];
+      carry_k += scan_s[1][0] + scan_s[1][1] + scan_s[1][2] + scan_s[1][3];
+      __syncthreads();
+    }
+    for (int i = carry_q + static_cast<int>(threadIdx.x); i < p.tab_q_len; i += 128)
+      p.tab_q[2 * i] = make_int4(-1, 0, 0, 0);
+    for (int i = carry_k + static_cast<int>(threadIdx.x); i < p.tab_k_len; i += 128)
+      p.tab_k[2 * i] = make_int4(-1, 0, 0, 0);
+  }
   {
     // Delta = rowsum(dO * O): a row is read by D/8 lanes (16 bytes each), so every
     // load instruction covers whole rows; each warp owns 32 of the block's rows.
@@ -353,9 +413,18 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
   float* vec = reinterpret_cast<float*>(smem + L::oVec);
 
   const ProblemDev& P = p.prob;
-  const int n_blk = blockIdx.x;
   const int hk = blockIdx.y;
-  const SeqInfo si = seq_info(P, blockIdx.z);
+  int n_blk;
+  SeqInfo si;
+  if (P.varlen) {  // one CTA per real key tile (table written by the pre kernel)
+    const int4 e0 = p.tab_k[2 * blockIdx.x], e1 = p.tab_k[2 * blockIdx.x + 1];
+    if (e0.x < 0) return;
+    n_blk = e0.x;
+    si.q_start = e0.y, si.k_start = e0.z, si.len_q = e0.w, si.len_k = e1.x, si.b = 0;
+  } else {
+    n_blk = blockIdx.x;
+    si = seq_info(P, blockIdx.z);
+  }
   const int n0 = n_blk * kBlockN;
   if (n0 >= si.len_k) return;
   const int g = P.heads / P.heads_kv;
@@ -831,9 +900,18 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::oMisc + 4);
 
   const ProblemDev& P = p.prob;
-  const int m_blk = p.n_mblocks - 1 - static_cast<int>(blockIdx.x);
   const int h = blockIdx.y;
-  const SeqInfo si = seq_info(P, blockIdx.z);
+  int m_blk;
+  SeqInfo si;
+  if (P.varlen) {  // one CTA per real query tile (table written by the pre kernel)
+    const int4 e0 = p.tab_q[2 * blockIdx.x], e1 = p.tab_q[2 * blockIdx.x + 1];
+    if (e0.x < 0) return;
+    m_blk = e0.x;
+    si.q_start = e0.y, si.k_start = e0.z, si.len_q = e0.w, si.len_k = e1.x, si.b = 0;
+  } else {
+    m_blk = p.n_mblocks - 1 - static_cast<int>(blockIdx.x);
+    si = seq_info(P, blockIdx.z);
+  }
   const int q0 = m_blk * kBlockM;
   if (q0 >= si.len_q) return;
   const int hk = h / (P.heads / P.heads_kv);
@@ -1212,7 +1290,7 @@ cudaError_t launch_bwd_t(const BwdMaps& m, const BwdParams& p, cudaStream_t stre
     auto kern = fna2_bwd_dkdv_kernel<D, RP>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
     if (e != cudaSuccess) return e;
-    dim3 grid(p.n_nblocks, p.prob.heads_kv, p.batch);
+    dim3 grid(p.prob.varlen ? p.tab_k_len : p.n_nblocks, p.prob.heads_kv, p.prob.varlen ? 1 : p.batch);
     kern<<<grid, kDkdvThreads, L::kTotal, stream>>>(m.qS, m.k, m.v, m.dOS, m.rqS, m.rk, p);
     e = cudaGetLastError();
     if (e == cudaSuccess && ev) e = cudaEventRecord(ev[2], stream);
@@ -1223,7 +1301,7 @@ cudaError_t launch_bwd_t(const BwdMaps& m, const BwdParams& p, cudaStream_t stre
     auto kern = fna2_bwd_dq_kernel<D, RP>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
     if (e != cudaSuccess) return e;
-    dim3 grid(p.n_mblocks, p.prob.heads, p.batch);
+    dim3 grid(p.prob.varlen ? p.tab_q_len : p.n_mblocks, p.prob.heads, p.prob.varlen ? 1 : p.batch);
     kern<<<grid, kDqThreads, L::kTotal, stream>>>(m.q, m.k112, m.v112, m.dO, m.rq, m.rk112, p);
     e = cudaGetLastError();
     if (e == cudaSuccess && ev) e = cudaEventRecord(ev[3], stream);

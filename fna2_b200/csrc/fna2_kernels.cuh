@@ -94,6 +94,12 @@ struct BwdParams {
   const __nv_bfloat16* rq;  // raw R_q rows (for d_gs = sum R_q * dS R_k)
   int64_t rq_sb, rq_sh, rq_sr;
   float* dgs;               // [H_G], accumulated with atomics (zeroed by the pre kernel)
+  // varlen: tables of the real tiles, 8 ints per entry {tile, q_start, k_start, len_q,
+  // len_k, 0, 0, 0} (tile < 0: past the end), written by the pre kernel; the dQ kernel
+  // launches tab_q_len CTAs per head (query tiles), the dK/dV kernel tab_k_len (key tiles)
+  int4* tab_q;
+  int4* tab_k;
+  int tab_q_len, tab_k_len;
   int total_q_rows;         // rows of q per (b,h) slot: dense S, varlen T
   int total_k_rows;
   int batch;                // dense B or varlen N

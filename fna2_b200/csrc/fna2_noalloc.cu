@@ -2,7 +2,8 @@
 // memory.
 //
 // fna2_bwd needs a caller-provided scratch buffer (the log2-domain LSE and
-// Delta = rowsum(dO*O) rows, 8 bytes per query row and head).  Some callers
+// Delta = rowsum(dO*O) rows, 8 bytes per query row and head, plus for packed
+// batches 32 bytes per query tile and per key tile).  Some callers
 // cannot provide one: processes whose device memory is entirely owned by
 // another allocator (a framework's caching pool or a fixed arena sized at
 // start-up, where an extra cudaMalloc would fail or fragment the arena), and
@@ -100,11 +101,12 @@ extern "C" int fna2_bwd_noalloc(const Fna2BwdArgs* a, void* stream) {
     if (int rc = check_tensor(a->dr_k, "dr_k", s.varlen)) return rc;
     FNA2_CHECK(a->graph_scale != nullptr && a->d_graph_scale != nullptr, "graph_scale/d_graph_scale: null");
   }
-  const size_t need = bwd_workspace_bytes(s.batch_dim(), s.H, s.HG, s.rows_q());
+  const size_t need = bwd_workspace_bytes(s.batch_dim(), s.H, s.HG, s.rows_q(), s.varlen, s.rows_k(), s.B);
   if (need > static_cast<size_t>(FNA2_NOALLOC_SCRATCH_BYTES))
     return fail(FNA2_ERR_WORKSPACE,
                 "fna2_bwd_noalloc: problem needs %zu bytes of scratch (8 bytes per query row and head, "
-                "batch*heads*rows = %lld) but the static scratch holds %d bytes; use fna2_bwd with a workspace",
+                "batch*heads*rows = %lld, plus the tile tables of packed batches) but the static scratch holds "
+                "%d bytes; use fna2_bwd with a workspace",
                 need, static_cast<long long>(s.batch_dim()) * s.H * s.rows_q(), FNA2_NOALLOC_SCRATCH_BYTES);
   void* scratch = nullptr;
   if (int rc = noalloc_scratch(&scratch)) return rc;
@@ -183,7 +185,7 @@ extern "C" int fna2_bwd_noalloc(const Fna2BwdArgs* a, void* stream) {
   p.batch = s.B;
   p.n_mblocks = (s.Sq + kBlockM - 1) / kBlockM;
   p.n_nblocks = (s.Sk + kBlockN - 1) / kBlockN;
-  bwd_set_workspace(&p, scratch, s.batch_dim(), s.H, s.rows_q());
+  bwd_set_workspace(&p, scratch, s.batch_dim(), s.H, s.rows_q(), s.varlen, s.rows_k(), s.B);
   FNA2_CUDA(launch_bwd(s.D, s.RP, mp, p, static_cast<cudaStream_t>(stream),
                        reinterpret_cast<cudaEvent_t*>(a->launch_events)));
   return FNA2_OK;

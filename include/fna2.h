@@ -120,7 +120,8 @@ int fna2_bwd(const Fna2BwdArgs* args, void* stream);
 /* Backward for callers that cannot allocate device memory (no counterpart in
  * the reference, which always allocates through PyTorch).  Same arguments and
  * results as fna2_bwd, but args->workspace / workspace_bytes are ignored: the
- * scratch (8 bytes per query row and head) comes from a static device array of
+ * scratch (8 bytes per query row and head, plus 32 bytes per 128-row query
+ * tile and per 128-row key tile of packed batches) comes from a static device array of
  * FNA2_NOALLOC_SCRATCH_BYTES held by every GPU that loads the library until
  * exit.  Larger problems return FNA2_ERR_WORKSPACE.  The first call on each
  * device looks the array up (cudaGetSymbolAddress); make it before any stream
