@@ -19,7 +19,8 @@ FNA2_ERR_CUDA = -2
 FNA2_ERR_WORKSPACE = -3
 
 EXPORTED = ["fna2_fwd", "fna2_bwd", "fna2_bwd_workspace_size", "fna2_last_error", "fna2_device_status",
-            "fna2_abi_version", "fna2_bwd_noalloc", "fna2_qk_prep_fwd", "fna2_qk_prep_bwd", "fna2_decode", "fna2_decode_workspace_size"]
+            "fna2_abi_version", "fna2_bwd_noalloc", "fna2_qk_prep_fwd", "fna2_qk_prep_bwd", "fna2_decode", "fna2_decode_workspace_size",
+            "fna2_debug_watchdog"]
 FNA2_DTYPE_F32 = 0
 FNA2_DTYPE_BF16 = 1
 NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024  # FNA2_NOALLOC_SCRATCH_BYTES
@@ -181,6 +182,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.fna2_last_error.restype = ctypes.c_char_p
     lib.fna2_device_status.argtypes = [ctypes.c_int]
     lib.fna2_device_status.restype = ctypes.c_int
+    lib.fna2_debug_watchdog.argtypes = [ctypes.c_int, ctypes.c_ulonglong]
+    lib.fna2_debug_watchdog.restype = ctypes.c_int
     lib.fna2_abi_version.argtypes = []
     lib.fna2_abi_version.restype = ctypes.c_int
     v = lib.fna2_abi_version()

@@ -155,6 +155,8 @@ ProblemDev to_dev(const Fna2Problem& p, const Shape& s) {
   d.rank = s.r;
   d.seqlen_q = s.Sq;
   d.seqlen_k = s.Sk;
+  d.total_q = s.varlen ? s.Tq : s.Sq;
+  d.total_k = s.varlen ? s.Tk : s.Sk;
   d.varlen = s.varlen ? 1 : 0;
   d.causal = s.varlen ? 1 : (p.causal ? 1 : 0);
   d.cu_q = p.cu_seqlens_q;
@@ -209,6 +211,16 @@ extern "C" int fna2_device_status(int reset) {
   return v;
 }
 
+extern "C" int fna2_debug_watchdog(int withhold_site, unsigned long long wait_limit_ns) {
+  g_last_error.clear();
+  FNA2_CHECK(withhold_site == 0 || withhold_site == kSiteFwdPFull, "withhold_site must be 0 or %d", kSiteFwdPFull);
+  const uint64_t limit = wait_limit_ns ? static_cast<uint64_t>(wait_limit_ns) : kWaitTimeoutNs;
+  FNA2_CUDA(cudaDeviceSynchronize());
+  FNA2_CUDA(cudaMemcpyToSymbol(g_wait_limit_ns, &limit, sizeof(limit)));
+  FNA2_CUDA(cudaMemcpyToSymbol(g_debug_withhold, &withhold_site, sizeof(int)));
+  return FNA2_OK;
+}
+
 extern "C" int fna2_fwd(const Fna2FwdArgs* a, void* stream) {
   g_last_error.clear();
   FNA2_CHECK(a != nullptr, "null args");
@@ -261,29 +273,39 @@ extern "C" size_t fna2_bwd_workspace_size(const Fna2Problem* prob) {
   return bwd_workspace_bytes(s.batch_dim(), s.H, s.HG, s.rows_q(), s.varlen, s.rows_k(), s.B);
 }
 
-extern "C" int fna2_bwd(const Fna2BwdArgs* a, void* stream) {
-  g_last_error.clear();
+namespace fna2 {
+namespace {
+
+// Argument checks shared by fna2_bwd and fna2_bwd_noalloc.  *empty is set when
+// the problem has no rows (nothing to launch).
+int bwd_check_args(const Fna2BwdArgs* a, Shape* s, bool* empty) {
   FNA2_CHECK(a != nullptr, "null args");
-  Shape s;
-  if (int rc = check_problem(a->prob, &s)) return rc;
-  if (s.B == 0 || s.Sq == 0) return FNA2_OK;
+  if (int rc = check_problem(a->prob, s)) return rc;
+  *empty = s->B == 0 || s->Sq == 0;
+  if (*empty) return FNA2_OK;
   const char* names[] = {"q", "k", "v", "out", "dout", "dq", "dk", "dv"};
   const Fna2Tensor* ts[] = {&a->q, &a->k, &a->v, &a->out, &a->dout, &a->dq, &a->dk, &a->dv};
   for (int i = 0; i < 8; ++i)
-    if (int rc = check_tensor(*ts[i], names[i], s.varlen)) return rc;
+    if (int rc = check_tensor(*ts[i], names[i], s->varlen)) return rc;
   FNA2_CHECK(a->lse != nullptr, "lse: null pointer");
-  if (s.HG > 0) {
-    if (int rc = check_tensor(a->r_q, "r_q", s.varlen)) return rc;
-    if (int rc = check_tensor(a->r_k, "r_k", s.varlen)) return rc;
-    if (int rc = check_tensor(a->dr_q, "dr_q", s.varlen)) return rc;
-    if (int rc = check_tensor(a->dr_k, "dr_k", s.varlen)) return rc;
+  if (s->HG > 0) {
+    if (int rc = check_tensor(a->r_q, "r_q", s->varlen)) return rc;
+    if (int rc = check_tensor(a->r_k, "r_k", s->varlen)) return rc;
+    if (int rc = check_tensor(a->dr_q, "dr_q", s->varlen)) return rc;
+    if (int rc = check_tensor(a->dr_k, "dr_k", s->varlen)) return rc;
     FNA2_CHECK(a->graph_scale != nullptr && a->d_graph_scale != nullptr, "graph_scale/d_graph_scale: null");
   }
-  const size_t need = bwd_workspace_bytes(s.batch_dim(), s.H, s.HG, s.rows_q(), s.varlen, s.rows_k(), s.B);
-  if (a->workspace_bytes < need || (need && a->workspace == nullptr))
-    return fail(FNA2_ERR_WORKSPACE, "workspace too small: %zu < %zu bytes", a->workspace_bytes, need);
-  FNA2_CHECK((reinterpret_cast<uintptr_t>(a->workspace) & 255u) == 0, "workspace must be 256-byte aligned");
+  return FNA2_OK;
+}
 
+size_t bwd_scratch_bytes(const Shape& s) {
+  return bwd_workspace_bytes(s.batch_dim(), s.H, s.HG, s.rows_q(), s.varlen, s.rows_k(), s.B);
+}
+
+// Tensor maps and kernel parameters of a checked backward call, with `scratch`
+// (bwd_scratch_bytes(s) bytes, 256-byte aligned) as its workspace; then the
+// three launches on `stream`.
+int bwd_launch(const Fna2BwdArgs* a, const Shape& s, void* scratch, void* stream) {
   BwdMaps m;
   if (int rc = map_qkv(&m.q, a->q, s, s.rows_q(), s.H, "q")) return rc;
   if (int rc = map_qkv(&m.k, a->k, s, s.rows_k(), s.HKV, "k")) return rc;
@@ -342,10 +364,26 @@ extern "C" int fna2_bwd(const Fna2BwdArgs* a, void* stream) {
   p.batch = s.B;
   p.n_mblocks = (s.Sq + kBlockM - 1) / kBlockM;
   p.n_nblocks = (s.Sk + kBlockN - 1) / kBlockN;
-  bwd_set_workspace(&p, a->workspace, s.batch_dim(), s.H, s.rows_q(), s.varlen, s.rows_k(), s.B);
+  bwd_set_workspace(&p, scratch, s.batch_dim(), s.H, s.rows_q(), s.varlen, s.rows_k(), s.B);
   FNA2_CUDA(launch_bwd(s.D, s.RP, m, p, static_cast<cudaStream_t>(stream),
                        reinterpret_cast<cudaEvent_t*>(a->launch_events)));
   return FNA2_OK;
+}
+
+}  // namespace
+}  // namespace fna2
+
+extern "C" int fna2_bwd(const Fna2BwdArgs* a, void* stream) {
+  g_last_error.clear();
+  Shape s;
+  bool empty = false;
+  if (int rc = bwd_check_args(a, &s, &empty)) return rc;
+  if (empty) return FNA2_OK;
+  const size_t need = bwd_scratch_bytes(s);
+  if (a->workspace_bytes < need || (need && a->workspace == nullptr))
+    return fail(FNA2_ERR_WORKSPACE, "workspace too small: %zu < %zu bytes", a->workspace_bytes, need);
+  FNA2_CHECK((reinterpret_cast<uintptr_t>(a->workspace) & 255u) == 0, "workspace must be 256-byte aligned");
+  return bwd_launch(a, s, a->workspace, stream);
 }
 
 // The no-allocation backward entry point (fna2_bwd_noalloc) and its static scratch.

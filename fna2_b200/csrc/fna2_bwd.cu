@@ -92,9 +92,16 @@ __global__ void __launch_bounds__(128) fna2_bwd_pre_kernel(const BwdParams p) {
       const int z = base + static_cast<int>(threadIdx.x);
       int qs = 0, ks = 0, lq = 0, lk = 0;
       if (z < p.batch) {
-        qs = __ldg(P.cu_q + z), lq = __ldg(P.cu_q + z + 1) - qs;
-        ks = __ldg(P.cu_k + z), lk = __ldg(P.cu_k + z + 1) - ks;
+        SeqInfo e;
+        e.q_start = __ldg(P.cu_q + z), e.len_q = __ldg(P.cu_q + z + 1) - e.q_start;
+        e.k_start = __ldg(P.cu_k + z), e.len_k = __ldg(P.cu_k + z + 1) - e.k_start;
+        if (seq_ok(P, e)) {
+          qs = e.q_start, lq = e.len_q, ks = e.k_start, lk = e.len_k;
+        } else {  // inconsistent cu_seqlens: the sequence gets no tiles (no access is made for it)
+          atomicCAS(&g_device_error, 0, kStatusBadSeqBwd);
+        }
       }
+      // lq, lk >= 0 here, so every table offset below stays in [0, tab_len)
       const int tq = (lq + kBlockM - 1) / kBlockM, tk = (lk + kBlockN - 1) / kBlockN;
       int iq = tq, ik = tk;  // inclusive scans within the warp
 #pragma unroll
@@ -106,7 +113,7 @@ __global__ void __launch_bounds__(128) fna2_bwd_pre_kernel(const BwdParams p) {
       __syncthreads();
       int oq = carry_q + iq - tq, ok = carry_k + ik - tk;
       for (int i = 0; i < w; ++i) oq += scan_s[0][i], ok += scan_s[1][i];
-      for (int t = 0; t < tq && oq + t < p.tab_q_len; ++t) {  // (bounded even for inconsistent cu_seqlens)
+      for (int t = 0; t < tq && oq + t < p.tab_q_len; ++t) {
         p.tab_q[2 * (oq + t)] = make_int4(tq - 1 - t, qs, ks, lq);
         p.tab_q[2 * (oq + t) + 1] = make_int4(lk, z, 0, 0);
       }
@@ -561,7 +568,7 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
       const int e = it / n_it;
       if (e < gh && (it % n_it) == 0) {
         // a new graph head: R~_k = R_k * gs/scale in place (element-wise, any swizzle)
-        if (!mbar_wait(&bars[kARkFull], e & 1, abort_flag, 602)) {
+        if (!mbar_wait(&bars[kARkFull], e & 1, abort_flag, 652)) {
           ok = false;
           break;
         }
@@ -573,7 +580,7 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
       }
       if (it + 1 < total_it) fetch(it + 1, nl2, ndl);
       // the Q load of tile it implies the stage's previous readers (tile it-3) are done
-      if (!mbar_wait(&bars[kAQFull + s], (it / L::kQStages) & 1, abort_flag, 601)) {
+      if (!mbar_wait(&bars[kAQFull + s], (it / L::kQStages) & 1, abort_flag, 651)) {
         ok = false;
         break;
       }

@@ -113,6 +113,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int pair = n_pairs - 1 - static_cast<int>(blockIdx.x);  // heaviest causal tiles first
   const int h = blockIdx.y;
   const SeqInfo si = seq_info(P, blockIdx.z);
+  if (!seq_ok(P, si)) {  // inconsistent cu_seqlens: skip the sequence, report it once
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) atomicCAS(&g_device_error, 0, kStatusBadSeqFwd);
+    return;
+  }
   const int q0 = pair * 2 * kBlockM;
   if (q0 >= si.len_q) return;
   const int hk = h / (P.heads / P.heads_kv);
@@ -304,6 +308,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int n_my = wi ? n_t[1] : n_t[0];
     const float sl2 = P.scale_log2;
     bool ok = true;
+    // watchdog test hook: tile 0 withholds its first P hand-off (never set in normal use)
+    const bool withhold = wi == 0 && *reinterpret_cast<volatile int*>(&g_debug_withhold) == kSiteFwdPFull;
 
     if (graph && n_my > 0) {
       // R~_q = R_q * gs/scale in place (element-wise, so independent of the swizzle).
@@ -400,7 +406,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[kBarPFull + wi]);
+      if (lane == 0 && !(withhold && j == 0)) mbar_arrive(&bars[kBarPFull + wi]);
     }
 
     if (ok && n_my > 0 && mbar_wait(&bars[kBarAllDone], 0, abort_flag, 304)) {

@@ -30,6 +30,7 @@ struct SeqInfo {
 struct ProblemDev {
   int heads, heads_kv, heads_graph, head_dim, rank;
   int seqlen_q, seqlen_k;  // dense lengths; varlen: max lengths (grid sizing only)
+  int total_q, total_k;    // varlen: rows of the packed q and k/v tensors
   int varlen, causal;
   const int* cu_q;
   const int* cu_k;
@@ -54,6 +55,22 @@ __device__ __forceinline__ SeqInfo seq_info(const ProblemDev& p, int bz) {
     s.b = bz;
   }
   return s;
+}
+
+// Site codes a kernel records in g_device_error (read by fna2_device_status)
+// when a packed sequence's cu_seqlens entries are inconsistent: a negative
+// length, rows outside the packed tensors, or a length above max_seqlen (the
+// bound the grids are sized by).  The sequence is skipped before any access.
+constexpr int kStatusBadSeqFwd = 621;  // found by the forward kernel
+constexpr int kStatusBadSeqBwd = 622;  // found by the backward pre-pass (tile tables)
+
+// A packed sequence the kernels may process: inside the packed tensors and no
+// longer than the max_seqlen bounds.  Dense problems always pass.
+__device__ __forceinline__ bool seq_ok(const ProblemDev& p, const SeqInfo& s) {
+  if (!p.varlen) return true;
+  const int64_t qe = static_cast<int64_t>(s.q_start) + s.len_q, ke = static_cast<int64_t>(s.k_start) + s.len_k;
+  return s.q_start >= 0 && s.len_q >= 0 && qe <= p.total_q && s.len_q <= p.seqlen_q && s.k_start >= 0 &&
+         s.len_k >= 0 && ke <= p.total_k && s.len_k <= p.seqlen_k;
 }
 
 struct FwdParams {

@@ -25,6 +25,14 @@ __device__ int g_device_error = 0;
 // Wait budget of one mbarrier wait before the kernel gives up (nanoseconds).
 constexpr uint64_t kWaitTimeoutNs = 4000000000ull;
 
+// Test hooks, set only through fna2_debug_watchdog(): the wait budget in use
+// (kWaitTimeoutNs unless a test shortens it) and the site code of one
+// mbarrier arrival that a kernel withholds so that the matching wait runs out
+// (0 = none; the forward kernel supports kSiteFwdPFull).
+__device__ uint64_t g_wait_limit_ns = kWaitTimeoutNs;
+__device__ int g_debug_withhold = 0;
+constexpr int kSiteFwdPFull = 204;  // the forward MMA thread's wait for P of query tile 0
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -64,19 +72,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Slow path of a bounded wait: spins on try_wait until the phase completes,
-// the CTA-wide abort flag is raised by another role, or kWaitTimeoutNs passes.
+// the CTA-wide abort flag is raised by another role, or the wait budget
+// (g_wait_limit_ns, 4 s) passes.  A wait gives up only long after every copy
+// and MMA that the CTA issued before it has completed, so the teardown that
+// follows (TMEM deallocation, exit) has nothing in flight.
 // On timeout it raises the abort flag and records `site` in g_device_error.
 // The abort flag and the timer are checked once per 32 suspending try_waits,
 // so a phase that completes is noticed with the hardware's wake-up latency.
 __device__ __noinline__ static bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                                    int site) {
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = *reinterpret_cast<volatile uint64_t*>(&g_wait_limit_ns);
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+    if (globaltimer_ns() - t0 > limit) {
       *abort_flag = 1;
       atomicCAS(&g_device_error, 0, site);
       return false;
@@ -110,12 +122,13 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 __device__ __noinline__ static bool mbar_spin_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                                    int site) {
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = *reinterpret_cast<volatile uint64_t*>(&g_wait_limit_ns);
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 256; ++i)
       if (mbar_test_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+    if (globaltimer_ns() - t0 > limit) {
       *abort_flag = 1;
       atomicCAS(&g_device_error, 0, site);
       return false;

@@ -14,9 +14,12 @@ Public surface kept verbatim (myAiByMe/FNA2):
   op itself accepts any rank r in {8, 16, 24, 32} (the reference asserts
   ``r == BLOCK_R``, :1423-1427).
 
-Behind it, every call goes through the C ABI of ``libfna2_b200.so``
-(include/fna2.h) to hand-written sm_100a kernels; there is no Triton, no
-eager fallback and no CPU path.  Tensors must live on a CUDA device.
+Behind it, the op is registered with PyTorch as the custom ops ``fna2::fwd``
+and ``fna2::bwd`` (torch.library; fake kernels for shape inference, the
+backward as the forward's autograd formula), whose CUDA implementations call
+the C ABI of ``libfna2_b200.so`` (include/fna2.h) to hand-written sm_100a
+kernels; there is no Triton, no eager fallback and no CPU path.  Tensors must
+live on a CUDA device.
 """
 from __future__ import annotations
 
@@ -98,7 +101,8 @@ def _stream() -> ctypes.c_void_p:
 
 
 def _validate(q, k, v, r_q, r_k, graph_scale, cu_q, cu_k):
-    if not q.is_cuda:
+    # meta tensors carry shapes only (tracing, shape inference); data must be on a CUDA device
+    if q.device.type not in ("cuda", "meta"):
         raise RuntimeError("flash_naylis_attn: tensors must be on a CUDA device (no CPU implementation)")
     dev = q.device
     for name, t in (("k", k), ("v", v), ("r_q", r_q), ("r_k", r_k), ("graph_scale", graph_scale)):
@@ -142,15 +146,17 @@ def _events_arg(events):
 
 
 def _fna2_forward(q, k, v, r_q, r_k, gs, softmax_scale, is_causal, cu_q=None, cu_k=None, max_q=0, max_k=0,
-                  launch_events=None) -> Tuple[torch.Tensor, torch.Tensor]:
+                  launch_events=None, out=None) -> Tuple[torch.Tensor, torch.Tensor]:
     """Forward launcher; replaces _fna2_forward / _fna2_forward_varlen
-    (flash_naylis_attn.py:700-804).  Returns (out, lse); lse is [B,H,S] dense
-    or [H,T] packed (fp32)."""
+    (flash_naylis_attn.py:700-804).  Inputs must be TMA-addressable
+    (``_prep``), ``gs`` fp32.  Returns (out, lse); lse is [B,H,S] dense or
+    [H,T] packed (fp32).  ``out`` may be given (a TMA-addressable buffer)."""
     lib = _lib.load()
     varlen = cu_q is not None
-    out = torch.empty_like(q)
-    if not _tma_ok(out):
-        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    if out is None:
+        out = torch.empty_like(q)
+        if not _tma_ok(out):
+            out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
     if varlen:
         lse = torch.empty(q.shape[1], q.shape[0], dtype=torch.float32, device=q.device)
     else:
@@ -168,15 +174,17 @@ def _fna2_forward(q, k, v, r_q, r_k, gs, softmax_scale, is_causal, cu_q=None, cu
 
 
 def _fna2_backward(dout, q, k, v, r_q, r_k, gs, out, lse, softmax_scale, is_causal, cu_q=None, cu_k=None,
-                   max_q=0, max_k=0, launch_events=None):
+                   max_q=0, max_k=0, launch_events=None, grads=None):
     """Backward launcher; replaces _fna2_backward / _fna2_backward_varlen
-    (flash_naylis_attn.py:807-892, :1215-1300).  Returns
-    (dq, dk, dv, dr_q, dr_k, d_gs)."""
+    (flash_naylis_attn.py:807-892, :1215-1300).  Inputs must be
+    TMA-addressable, ``gs`` fp32.  Returns (dq, dk, dv, dr_q, dr_k, d_gs);
+    ``grads`` may give the five bf16 gradient buffers."""
     lib = _lib.load()
     varlen = cu_q is not None
     dout = _prep(dout)
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    dr_q, dr_k = torch.empty_like(r_q), torch.empty_like(r_k)
+    if grads is None:
+        grads = [torch.empty_like(t) for t in (q, k, v, r_q, r_k)]
+    dq, dk, dv, dr_q, dr_k = grads
     hg = r_q.shape[1]
     d_gs = torch.empty(hg, dtype=torch.float32, device=q.device)
     a = _lib.Fna2BwdArgs()
@@ -199,38 +207,131 @@ def _fna2_backward(dout, q, k, v, r_q, r_k, gs, out, lse, softmax_scale, is_caus
 
 
 # ---------------------------------------------------------------------------
+# PyTorch custom ops fna2::fwd / fna2::bwd over the C ABI
+# ---------------------------------------------------------------------------
+# Registered with torch.library so that the op is a node of its own in
+# torch.compile / export graphs (no graph break at the call), with fake
+# (meta) kernels for shape inference and the backward registered as its
+# autograd formula.  The real kernels run on CUDA devices only.
+
+def _out_like(t: torch.Tensor) -> torch.Tensor:
+    """Output buffer with ``t``'s layout (``empty_like``, as the reference's
+    launchers allocate, flash_naylis_attn.py:722-723,835-840)."""
+    return torch.empty_like(t)
+
+
+def _kernel_view(buf: torch.Tensor) -> torch.Tensor:
+    """The buffer itself when TMA can address it, else a contiguous stand-in
+    whose result is copied back by _finish."""
+    return buf if _tma_ok(buf) else torch.empty(buf.shape, dtype=buf.dtype, device=buf.device)
+
+
+def _finish(buf: torch.Tensor, k: torch.Tensor) -> torch.Tensor:
+    if k is not buf:
+        buf.copy_(k)
+    return buf
+
+
+def _lse_shape(q: torch.Tensor, varlen: bool):
+    return (q.shape[1], q.shape[0]) if varlen else (q.shape[0], q.shape[1], q.shape[2])
+
+
+@torch.library.custom_op("fna2::fwd", mutates_args=(), device_types="cuda")
+def fna2_fwd_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, r_q: torch.Tensor, r_k: torch.Tensor,
+                graph_scale: torch.Tensor, softmax_scale: float, is_causal: bool,
+                cu_seqlens_q: Optional[torch.Tensor], cu_seqlens_k: Optional[torch.Tensor],
+                max_seqlen_q: int, max_seqlen_k: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Forward (flash_naylis_attn.py:700-804): returns (out, lse); out has q's
+    shape, dtype and layout, lse is fp32 [B,H,S] dense or [H,T] packed."""
+    gs = graph_scale.to(torch.float32).contiguous()
+    qp, kp, vp, rqp, rkp = (_prep(t) for t in (q, k, v, r_q, r_k))
+    out = _out_like(q)
+    ko = _kernel_view(out)
+    lse = _fna2_forward(qp, kp, vp, rqp, rkp, gs, softmax_scale, is_causal, cu_seqlens_q, cu_seqlens_k,
+                        max_seqlen_q, max_seqlen_k, out=ko)[1]
+    return _finish(out, ko), lse
+
+
+@fna2_fwd_op.register_fake
+def _fna2_fwd_fake(q, k, v, r_q, r_k, graph_scale, softmax_scale, is_causal, cu_seqlens_q, cu_seqlens_k,
+                   max_seqlen_q, max_seqlen_k):
+    return torch.empty_like(q), q.new_empty(_lse_shape(q, cu_seqlens_q is not None), dtype=torch.float32)
+
+
+@torch.library.custom_op("fna2::bwd", mutates_args=(), device_types="cuda")
+def fna2_bwd_op(dout: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, r_q: torch.Tensor,
+                r_k: torch.Tensor, graph_scale: torch.Tensor, out: torch.Tensor, lse: torch.Tensor,
+                softmax_scale: float, is_causal: bool, cu_seqlens_q: Optional[torch.Tensor],
+                cu_seqlens_k: Optional[torch.Tensor], max_seqlen_q: int, max_seqlen_k: int
+                ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Backward (flash_naylis_attn.py:807-892, :1215-1300): returns
+    (dq, dk, dv, dr_q, dr_k, d_graph_scale), each in its input's dtype and
+    layout."""
+    gs = graph_scale.to(torch.float32).contiguous()
+    # dout.contiguous() in the reference (:1355); here only when TMA cannot read it
+    dp, qp, kp, vp, rqp, rkp, op = (_prep(t) for t in (dout, q, k, v, r_q, r_k, out))
+    bufs = [_out_like(t) for t in (q, k, v, r_q, r_k)]
+    kv = [_kernel_view(b) for b in bufs]
+    d_gs = _fna2_backward(dp, qp, kp, vp, rqp, rkp, gs, op, lse.contiguous(), softmax_scale, is_causal,
+                          cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, grads=kv)[5]
+    dq, dk, dv, dr_q, dr_k = (_finish(b, x) for b, x in zip(bufs, kv))
+    return dq, dk, dv, dr_q, dr_k, d_gs.to(graph_scale.dtype)
+
+
+@fna2_bwd_op.register_fake
+def _fna2_bwd_fake(dout, q, k, v, r_q, r_k, graph_scale, out, lse, softmax_scale, is_causal, cu_seqlens_q,
+                   cu_seqlens_k, max_seqlen_q, max_seqlen_k):
+    return (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty_like(r_q),
+            torch.empty_like(r_k), torch.empty_like(graph_scale))
+
+
+def _fwd_setup_context(ctx, inputs, output):
+    (q, k, v, r_q, r_k, graph_scale, softmax_scale, is_causal, cu_q, cu_k, max_q, max_k) = inputs
+    out, lse = output
+    ctx.save_for_backward(q, k, v, r_q, r_k, graph_scale, out, lse, cu_q, cu_k)
+    ctx.softmax_scale = softmax_scale
+    ctx.is_causal = is_causal
+    ctx.max_seqlen_q = max_q
+    ctx.max_seqlen_k = max_k
+
+
+def _fwd_backward(ctx, dout, dlse):
+    # lse is an auxiliary output; its gradient is not propagated (the
+    # reference's autograd Function returns out only, :1340)
+    q, k, v, r_q, r_k, graph_scale, out, lse, cu_q, cu_k = ctx.saved_tensors
+    grads = torch.ops.fna2.bwd(dout, q, k, v, r_q, r_k, graph_scale, out, lse, ctx.softmax_scale, ctx.is_causal,
+                               cu_q, cu_k, ctx.max_seqlen_q, ctx.max_seqlen_k)
+    return tuple(grads) + (None,) * 6
+
+
+fna2_fwd_op.register_autograd(_fwd_backward, setup_context=_fwd_setup_context)
+
+
+# ---------------------------------------------------------------------------
 # autograd Function and public op
 # ---------------------------------------------------------------------------
 
 class FlashNaylisAttnFunc(torch.autograd.Function):
-    """Autograd wrapper (flash_naylis_attn.py:1307-1373)."""
+    """Autograd wrapper with the reference's name and call signature
+    (flash_naylis_attn.py:1307-1373): ``apply(q, k, v, r_q, r_k, graph_scale,
+    softmax_scale, is_causal, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
+    max_seqlen_k)`` returns ``out``; backward returns six gradients and six
+    ``None``.  Both directions run the fna2::fwd / fna2::bwd custom ops."""
 
     @staticmethod
     def forward(ctx, q, k, v, r_q, r_k, graph_scale, softmax_scale: float, is_causal: bool,
                 cu_seqlens_q=None, cu_seqlens_k=None, max_seqlen_q: int = 0, max_seqlen_k: int = 0):
-        gs = graph_scale.detach().to(torch.float32).contiguous()
-        q, k, v, r_q, r_k = (_prep(t) for t in (q, k, v, r_q, r_k))
-        out, lse = _fna2_forward(q, k, v, r_q, r_k, gs, softmax_scale, is_causal,
-                                 cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k)
-        ctx.save_for_backward(q, k, v, r_q, r_k, gs, out, lse)
-        ctx.softmax_scale = softmax_scale
-        ctx.is_causal = is_causal
-        ctx.use_varlen = cu_seqlens_q is not None
-        ctx.cu_seqlens_q = cu_seqlens_q
-        ctx.cu_seqlens_k = cu_seqlens_k
-        ctx.max_seqlen_q = max_seqlen_q
-        ctx.max_seqlen_k = max_seqlen_k
-        ctx.gs_dtype = graph_scale.dtype
+        out, lse = torch.ops.fna2.fwd(q, k, v, r_q, r_k, graph_scale, softmax_scale, is_causal,
+                                      cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k)
+        ctx.save_for_backward(q, k, v, r_q, r_k, graph_scale, out, lse)
+        ctx.args = (softmax_scale, is_causal, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k)
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        q, k, v, r_q, r_k, gs, out, lse = ctx.saved_tensors
-        dout = dout.contiguous()
-        dq, dk, dv, dr_q, dr_k, d_gs = _fna2_backward(
-            dout, q, k, v, r_q, r_k, gs, out, lse, ctx.softmax_scale, ctx.is_causal,
-            ctx.cu_seqlens_q, ctx.cu_seqlens_k, ctx.max_seqlen_q, ctx.max_seqlen_k)
-        return dq, dk, dv, dr_q, dr_k, d_gs.to(ctx.gs_dtype), None, None, None, None, None, None
+        q, k, v, r_q, r_k, graph_scale, out, lse = ctx.saved_tensors
+        grads = torch.ops.fna2.bwd(dout, q, k, v, r_q, r_k, graph_scale, out, lse, *ctx.args)
+        return tuple(grads) + (None,) * 6
 
 
 def flash_naylis_attn(
@@ -257,7 +358,9 @@ def flash_naylis_attn(
     cu_seqlens_* : int32 [N+1] cumulative lengths (varlen mode when given)
     max_seqlen_* : upper bounds of the packed lengths (0 = unknown)
 
-    Returns ``out`` with q's shape and dtype.
+    Returns ``out`` with q's shape and dtype.  Runs the fna2::fwd custom op
+    (autograd: fna2::bwd), so it traces into torch.compile graphs without a
+    break.
     """
     if softmax_scale is None:
         softmax_scale = 1.0 / math.sqrt(q.shape[-1])
@@ -265,5 +368,6 @@ def flash_naylis_attn(
     assert r_q.dtype == torch.bfloat16, "r_q must be bfloat16"
     assert r_k.dtype == torch.bfloat16, "r_k must be bfloat16"
     _validate(q, k, v, r_q, r_k, graph_scale, cu_seqlens_q, cu_seqlens_k)
-    return FlashNaylisAttnFunc.apply(q, k, v, r_q, r_k, graph_scale, softmax_scale, is_causal,
-                                     cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k)
+    out, _ = torch.ops.fna2.fwd(q, k, v, r_q, r_k, graph_scale, float(softmax_scale), bool(is_causal),
+                                cu_seqlens_q, cu_seqlens_k, int(max_seqlen_q or 0), int(max_seqlen_k or 0))
+    return out

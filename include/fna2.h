@@ -237,10 +237,33 @@ int fna2_decode(const Fna2DecodeArgs* args, void* workspace, size_t workspace_by
 /* Message of the last failed call on this host thread ("" if none). */
 const char* fna2_last_error(void);
 
-/* Device watchdog: returns the site code recorded by a kernel whose bounded
- * mbarrier wait gave up (0 = none) and clears it when reset != 0.
- * Synchronises the current device. */
+/* Device status: returns the first site code a kernel recorded since the last
+ * reset (0 = none) and clears it when reset != 0.  Synchronises the current
+ * device.  Codes:
+ *   1xx-10xx  a bounded mbarrier wait gave up after its budget (4 s): the
+ *             kernel raised its CTA's abort flag, skipped the rest of the
+ *             tile and deallocated its tensor memory (hundreds digit = kernel
+ *             role: 1-3 forward, 4-7 dK/dV, 8-10 dQ);
+ *   199, 499  the dynamic shared memory base was not 1024-byte aligned;
+ *   601       decode: a cache length < 0 or above the capacity (zeros written);
+ *   621       forward, packed batch: a sequence with inconsistent cu_seqlens
+ *             (negative length, rows outside [0, total_q/total_k), or longer
+ *             than max_seqlen_q/_k); the sequence is skipped, its out/lse rows
+ *             are not written;
+ *   622       backward pre-pass, packed batch: the same check; the sequence
+ *             gets no tiles and its gradient rows are not written.
+ * Neither the reference nor this library checks cu_seqlens on the host (that
+ * would need a device-to-host copy per call). */
 int fna2_device_status(int reset);
+
+/* Testing hook (no counterpart in the reference): makes the forward kernel
+ * withhold one mbarrier arrival (withhold_site = 204: the first P hand-off of
+ * each CTA's first query tile) and sets the wait budget to wait_limit_ns
+ * (0 = the default 4 s), so that a test can check that a wait which runs out
+ * records its site code, that the kernel exits cleanly and that the next call
+ * works.  fna2_debug_watchdog(0, 0) restores normal operation.  Synchronises
+ * the current device. */
+int fna2_debug_watchdog(int withhold_site, unsigned long long wait_limit_ns);
 
 /* FNA2_ABI_VERSION of the loaded library. */
 int fna2_abi_version(void);

@@ -201,6 +201,95 @@ def varlen_bwd(q, k, v, r_q, r_k, gs, out, lse, dout, cu_q, cu_k, scale: float):
 
 
 # ----------------------------------------------------------------------------
+# blocked restatement for full-size checks (any device, fp32 arithmetic)
+# ----------------------------------------------------------------------------
+
+def blocked_sequence(q, k, v, r_q, r_k, gs, dout, scale: float, causal: bool = True, block: int = 512,
+                     grads: bool = True):
+    """Forward and backward of ONE sequence, the same formulas as
+    ``attention_fwd`` / ``attention_bwd`` (flash_naylis_attn.py:146-201,
+    356-693), evaluated over blocks of ``block`` query rows so that the score
+    matrix is never held beyond ``[H, block, L_k]``: full-size BASELINE
+    sequences (L up to 32768) fit on a GPU.  Arithmetic is fp32 on whatever
+    device the inputs live on (callers disable TF32).
+
+    Packed-slice layout: q/dout ``[L_q, H, D]``, k/v ``[L_k, H_KV, D]``,
+    r_q ``[L_q, H_G, r]``, r_k ``[L_k, H_G, r]``, gs ``[H_G]``.  Causal is
+    top-left aligned on local positions (key j visible to query i iff j <= i).
+    Returns a dict of out, lse ``[L_q, H]`` and, with ``grads``, dq, dk, dv,
+    drq, drk (input layouts) and dgs (fp64 sum, ``[H_G]``).
+    """
+    f32 = torch.float32
+    Lq, H, D = q.shape
+    Lk, HKV = k.shape[0], k.shape[1]
+    HG = r_q.shape[1]
+    g = H // HKV
+    dev = q.device
+    qf = q.to(f32).transpose(0, 1)                                   # [H, Lq, D]
+    kf = k.to(f32).transpose(0, 1).repeat_interleave(g, 0)           # [H, Lk, D]
+    vf = v.to(f32).transpose(0, 1).repeat_interleave(g, 0)
+    rqf = r_q.to(f32).transpose(0, 1)                                # [HG, Lq, r]
+    rkf = r_k.to(f32).transpose(0, 1)                                # [HG, Lk, r]
+    gsf = gs.to(f32).view(HG, 1, 1)
+    out = torch.zeros(H, Lq, D, dtype=f32, device=dev)
+    lse = torch.full((H, Lq), float("-inf"), dtype=f32, device=dev)
+
+    def logits(i0, i1):
+        kend = min(Lk, i1) if causal else Lk
+        s = scale * torch.matmul(qf[:, i0:i1], kf[:, :kend].transpose(1, 2))
+        if HG:
+            s[:HG] += gsf * torch.matmul(rqf[:, i0:i1], rkf[:, :kend].transpose(1, 2))
+        if causal:
+            ok = torch.arange(i0, i1, device=dev).view(-1, 1) >= torch.arange(kend, device=dev).view(1, -1)
+            s.masked_fill_(~ok, float("-inf"))
+        return s, kend
+
+    if Lk > 0:
+        for i0 in range(0, Lq, block):
+            i1 = min(Lq, i0 + block)
+            s, kend = logits(i0, i1)
+            m = s.amax(-1, keepdim=True)
+            m = torch.where(torch.isfinite(m), m, torch.zeros_like(m))
+            p = torch.exp(s - m)
+            l = p.sum(-1, keepdim=True)
+            out[:, i0:i1] = torch.matmul(p, vf[:, :kend]) / (l + EPS)          # :192
+            lse[:, i0:i1] = (m + torch.log(l + EPS)).squeeze(-1)               # :195
+    res = {"out": out.transpose(0, 1), "lse": lse.transpose(0, 1)}
+    if not grads:
+        return res
+    dof = dout.to(f32).transpose(0, 1)
+    delta = (dof * out).sum(-1, keepdim=True)                                   # :381
+    dq = torch.zeros_like(qf)
+    dk = torch.zeros(H, Lk, D, dtype=f32, device=dev)
+    dv = torch.zeros(H, Lk, D, dtype=f32, device=dev)
+    drq = torch.zeros_like(rqf)
+    drk = torch.zeros(HG, Lk, rkf.shape[-1], dtype=f32, device=dev)
+    dgs = torch.zeros(HG, dtype=torch.float64, device=dev)
+    if Lk > 0:
+        for i0 in range(0, Lq, block):
+            i1 = min(Lq, i0 + block)
+            s, kend = logits(i0, i1)
+            p = torch.exp(s - lse[:, i0:i1].unsqueeze(-1))                      # :518
+            p = torch.where(torch.isfinite(s), p, torch.zeros_like(p))
+            dp = torch.matmul(dof[:, i0:i1], vf[:, :kend].transpose(1, 2))     # :522
+            ds = p * (dp - delta[:, i0:i1])                                     # :523
+            dq[:, i0:i1] = scale * torch.matmul(ds, kf[:, :kend])              # :679
+            dk[:, :kend] += scale * torch.matmul(ds.transpose(1, 2), qf[:, i0:i1])   # :529
+            dv[:, :kend] += torch.matmul(p.transpose(1, 2), dof[:, i0:i1])     # :527
+            if HG:
+                dsg = ds[:HG]
+                drq[:, i0:i1] = gsf * torch.matmul(dsg, rkf[:, :kend])         # :683
+                drk[:, :kend] += gsf * torch.matmul(dsg.transpose(1, 2), rqf[:, i0:i1])  # :535
+                raw = torch.matmul(rqf[:, i0:i1], rkf[:, :kend].transpose(1, 2))
+                dgs += (dsg * raw).sum(dim=(1, 2)).double()                    # :537-538
+    res.update(dq=dq.transpose(0, 1),
+               dk=dk.view(HKV, g, Lk, D).sum(1).transpose(0, 1),
+               dv=dv.view(HKV, g, Lk, D).sum(1).transpose(0, 1),
+               drq=drq.transpose(0, 1), drk=drk.transpose(0, 1), dgs=dgs)
+    return res
+
+
+# ----------------------------------------------------------------------------
 # error metrics (validate_fna2.py:115-122 reports max/mean abs; rel-L2 added)
 # ----------------------------------------------------------------------------
 

@@ -1,7 +1,7 @@
 """Generate the golden fixtures under ``tests/golden/`` from the REFERENCE itself.
 
 Run in a container that has the reference source mounted (it is imported from
-``$FNA2_REFERENCE``, default: the mounted reference checkout's FNA2 directory); the fixtures it writes
+``$FNA2_REFERENCE``, required: the reference checkout's FNA2 directory); the fixtures it writes
 are committed, so nothing else ever needs the reference at run time.
 
 Two witnesses of the reference are recorded:
@@ -39,7 +39,10 @@ import torch  # noqa: E402
 
 from oracle import fna2_oracle as O  # noqa: E402
 
-REF = os.environ.get("FNA2_REFERENCE", "/root/reference/FNA2")
+REF = os.environ.get("FNA2_REFERENCE")
+if not REF:
+    raise SystemExit("set FNA2_REFERENCE to the reference checkout's FNA2 directory "
+                     "(the directory holding flash_naylis_attn.py)")
 
 
 def _hash(*ts):

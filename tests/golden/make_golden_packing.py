@@ -4,8 +4,8 @@ helpers.
 The reference ships pack_batch and pack_documents as Python code blocks in
 FNA2/INTEGRATION.md (:133-151 and :236-257).  This script takes each block's
 source text from that file, executes it, and records its outputs on seeded
-inputs and edge cases.  It needs the reference tree (FNA2_REFERENCE, default
-the reference checkout) and runs on CPU; the JSON it writes is what the tests
+inputs and edge cases.  It needs the reference tree (FNA2_REFERENCE, required:
+the reference checkout's FNA2 directory) and runs on CPU; the JSON it writes is what the tests
 read.
 
     python tests/golden/make_golden_packing.py
@@ -16,7 +16,10 @@ import random
 
 import torch
 
-REF = os.environ.get("FNA2_REFERENCE", "/root/reference/FNA2")
+REF = os.environ.get("FNA2_REFERENCE")
+if not REF:
+    raise SystemExit("set FNA2_REFERENCE to the reference checkout's FNA2 directory "
+                     "(the directory holding flash_naylis_attn.py)")
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "packing_cases.json")
 
 

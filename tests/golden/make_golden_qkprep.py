@@ -2,7 +2,7 @@
 REFERENCE's own classes (FNA2/attention_fna2.py: RMSNorm :94-102,
 RotaryPositionalEmbedding :108-170, NaylisAttention._apply_rope_varlen
 :620-647) on the CPU.  Run where the reference source is mounted
-(``$FNA2_REFERENCE``, default: the mounted reference checkout's FNA2 directory); the .pt files it writes
+(``$FNA2_REFERENCE``, required: the reference checkout's FNA2 directory); the .pt files it writes
 are committed.  Inputs are regenerated from seeds by
 ``oracle.qk_prep_oracle.make_inputs``; a SHA-256 of them is stored.
 
@@ -25,7 +25,10 @@ import torch  # noqa: E402
 
 from oracle import qk_prep_oracle as Q  # noqa: E402
 
-REF = os.environ.get("FNA2_REFERENCE", "/root/reference/FNA2")
+REF = os.environ.get("FNA2_REFERENCE")
+if not REF:
+    raise SystemExit("set FNA2_REFERENCE to the reference checkout's FNA2 directory "
+                     "(the directory holding flash_naylis_attn.py)")
 
 CASES = {
     # name: (lengths, H, H_KV, D, seed, dtype, lead, tail, yarn_scale, weights dtype)

@@ -7,32 +7,47 @@ import torch
 from oracle import fna2_oracle as O
 
 # Tolerance (bf16 kernel vs fp32/fp64 oracle on identical bf16-representable
-# inputs): relative L2 <= 1e-2 and max-abs <= 2e-2, the max-abs bound scaled by
-# the tensor's magnitude when that exceeds 1 (bf16 carries 8 significant bits,
-# so an element of size 4 is itself only representable to 1.6e-2).
+# inputs): relative L2 <= 1e-2 and max-abs <= 2e-2 (the north star's bf16
+# bound).  The flat max-abs bound is applied first.  Only where it fails on a
+# tensor whose values exceed 1 is it scaled by max|ref|: a bf16 value near 8
+# is itself only representable to 2^-5 = 0.031 (half-ULP 0.016), so rounding
+# the exact result to the bf16 output alone can exceed 2e-2 there.  Every
+# check is recorded in REPORT with the bound it used.
 REL_L2 = 1e-2
 MAX_ABS = 2e-2
 
 GRADS = ("dq", "dk", "dv", "drq", "drk", "dgs")
+
+REPORT = []  # one dict per check: name, max_abs, rel_l2, ref_max, bound, kind
 
 
 def check(name, ref, got, rel_l2=REL_L2, max_abs=MAX_ABS):
     ref = ref.detach().cpu()
     got = got.detach().float().cpu()
     e = O.errors(ref, got)
-    bound = max_abs * max(1.0, e["ref_max"])
     assert math.isfinite(e["max_abs"]), f"{name}: non-finite values {e}"
+    flat = e["max_abs"] <= max_abs
+    bound = max_abs if flat else max_abs * max(1.0, e["ref_max"])
     # relative L2 with a noise floor: a tensor whose true values are ~1e-6
     # (e.g. dQ of a single-token sequence, zero up to the +1e-6 normalisation)
     # is judged by max-abs alone
     floor = 1e-3 * math.sqrt(max(ref.numel(), 1))
     rel = (ref.double() - got.double()).norm().item() / max(ref.double().norm().item(), floor)
     e["rel_l2_floored"] = rel
+    REPORT.append({"name": name, "max_abs": e["max_abs"], "rel_l2": e["rel_l2"], "ref_max": e["ref_max"],
+                   "bound": bound, "kind": "flat" if flat else "scaled by max|ref|"})
     assert rel <= rel_l2 and e["max_abs"] <= bound, f"{name}: {e} (bound max_abs {bound:.3g})"
     return e
 
 
-def run_cuda(q, k, v, rq, rk, gs, do, scale, causal, cu=None, max_seqlen=0, backward=True):
+def record(name, max_abs, rel_l2, ref_max, bound, kind):
+    """Record an aggregate check made outside check() (streamed full-size tensors)."""
+    REPORT.append({"name": name, "max_abs": max_abs, "rel_l2": rel_l2, "ref_max": ref_max, "bound": bound,
+                   "kind": kind})
+
+
+def run_cuda(q, k, v, rq, rk, gs, do, scale, causal, cu=None, max_seqlen=0, backward=True, cu_k=None,
+             max_seqlen_k=None):
     """Call the drop-in op on CUDA copies; returns dict of CPU fp32 results."""
     from fna2_b200 import flash_naylis_attn
     dev = "cuda"
@@ -41,7 +56,9 @@ def run_cuda(q, k, v, rq, rk, gs, do, scale, causal, cu=None, max_seqlen=0, back
     kw = {}
     if cu is not None:
         cu_t = torch.tensor(cu, dtype=torch.int32, device=dev)
-        kw = dict(cu_seqlens_q=cu_t, cu_seqlens_k=cu_t, max_seqlen_q=max_seqlen, max_seqlen_k=max_seqlen)
+        cu_kt = cu_t if cu_k is None else torch.tensor(cu_k, dtype=torch.int32, device=dev)
+        msk = max_seqlen if max_seqlen_k is None else max_seqlen_k
+        kw = dict(cu_seqlens_q=cu_t, cu_seqlens_k=cu_kt, max_seqlen_q=max_seqlen, max_seqlen_k=msk)
     out = flash_naylis_attn(*t, g, softmax_scale=scale, is_causal=causal, **kw)
     res = {"out": out.detach().float().cpu()}
     if backward:
@@ -51,7 +68,7 @@ def run_cuda(q, k, v, rq, rk, gs, do, scale, causal, cu=None, max_seqlen=0, back
     return res
 
 
-def run_oracle(q, k, v, rq, rk, gs, do, scale, causal, cu=None, dtype=torch.float64, backward=True):
+def run_oracle(q, k, v, rq, rk, gs, do, scale, causal, cu=None, dtype=torch.float64, backward=True, cu_k=None):
     c = lambda x: x.to(dtype)
     if cu is None:
         out, lse = O.attention_fwd(c(q), c(k), c(v), c(rq), c(rk), c(gs), scale, causal)
@@ -60,10 +77,11 @@ def run_oracle(q, k, v, rq, rk, gs, do, scale, causal, cu=None, dtype=torch.floa
             g = O.attention_bwd(c(q), c(k), c(v), c(rq), c(rk), c(gs), out, lse, c(do), scale, causal)
             res.update(dict(zip(GRADS, g)))
     else:
-        out, lse = O.varlen_fwd(c(q), c(k), c(v), c(rq), c(rk), c(gs), cu, cu, scale)
+        ck = cu if cu_k is None else cu_k
+        out, lse = O.varlen_fwd(c(q), c(k), c(v), c(rq), c(rk), c(gs), cu, ck, scale)
         res = {"out": out, "lse": lse}
         if backward:
-            g = O.varlen_bwd(c(q), c(k), c(v), c(rq), c(rk), c(gs), out, lse, c(do), cu, cu, scale)
+            g = O.varlen_bwd(c(q), c(k), c(v), c(rq), c(rk), c(gs), out, lse, c(do), cu, ck, scale)
             res.update(dict(zip(GRADS, g)))
     return res
 

@@ -36,6 +36,34 @@ def test_oracle_matches_reference(name):
         assert e["rel_l2"] < 5e-6, (g, e)
 
 
+@pytest.mark.parametrize("name", CASES)
+def test_blocked_oracle_matches_reference(name):
+    """The blocked restatement used by the full-size GPU checks
+    (oracle.fna2_oracle.blocked_sequence, fp32) reproduces the same golden
+    vectors, with a block size that splits every case into several blocks."""
+    rec, (q, k, v, rq, rk, gs, do, cu) = load(name)
+    if rec["kind"] == "dense":
+        seqs = [(b, None) for b in range(q.shape[0])]
+        sl = lambda t, b, _: t[b].transpose(0, 1)            # [H, S, X] -> [S, H, X]
+        put = lambda t, b, _: t[b].transpose(0, 1)
+    else:
+        seqs = [(cu[i], cu[i + 1]) for i in range(len(cu) - 1)]
+        sl = lambda t, a, b: t[a:b]
+        put = sl
+    dgs = torch.zeros_like(gs, dtype=torch.float64)
+    for a, b in seqs:
+        res = O.blocked_sequence(sl(q, a, b), sl(k, a, b), sl(v, a, b), sl(rq, a, b), sl(rk, a, b), gs,
+                                 sl(do, a, b), rec["scale"], rec["causal"], block=24)
+        for n in ("out", "dq", "dk", "dv", "drq", "drk"):
+            ref = put(rec[n], a, b)
+            if ref.numel():
+                e = O.errors(ref, res[n])
+                assert e["max_abs"] < 5e-5 and (e["rel_l2"] < 5e-6 or ref.abs().max() < 1e-3), (n, a, e)
+        dgs += res["dgs"]
+    e = O.errors(rec["dgs"], dgs)
+    assert e["rel_l2"] < 5e-6, e
+
+
 def test_oracle_autograd_agrees_with_explicit_backward():
     q, k, v, rq, rk, gs, do = O.make_dense_inputs(1, 4, 70, 32, 16, H_KV=2, H_G=2, seed=3, gs_value="randn")
     ts = [t.double().requires_grad_(True) for t in (q, k, v, rq, rk, gs)]

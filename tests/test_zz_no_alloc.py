@@ -13,6 +13,7 @@ every other test before this one.
 """
 import ctypes
 import math
+import threading
 
 import pytest
 import torch
@@ -91,6 +92,25 @@ def test_noalloc_backward_matches_workspace_backward_twice():
         torch.cuda.synchronize()
         for n in ref:
             parity.check(f"noalloc call {call + 1} {n}", ref[n], t[n])
+
+    # and once more from a host thread that has made no CUDA call yet: the
+    # scratch address is cached from the calls above, and the tensor maps
+    # still need the device's context bound on this new thread
+    _fresh_grads(t)
+    b = _bwd_args(prob, t, True)
+    b.workspace, b.workspace_bytes = None, 0
+    torch.cuda.synchronize()
+    rc = []
+    def call():  # fna2_last_error is per host thread: read it on the calling thread
+        rc.append((lib.fna2_bwd_noalloc(ctypes.byref(b), None), lib.fna2_last_error()))
+
+    th = threading.Thread(target=call)
+    th.start()
+    th.join()
+    assert rc and rc[0][0] == _lib.FNA2_OK, rc
+    torch.cuda.synchronize()
+    for n in ref:
+        parity.check(f"noalloc fresh-thread call {n}", ref[n], t[n])
     assert lib.fna2_device_status(1) == 0
 
 
