@@ -14,6 +14,10 @@ from tests import parity
 pytestmark = pytest.mark.gpu
 
 SITE_FWD_P = 204  # the forward MMA thread's wait for the first P hand-off
+# With that hand-off withheld, the first wait of the CTA to run out is either
+# the MMA thread's (204) or the softmax warps' wait for the end of the tile,
+# which can no longer come (304); both are sites of the forward kernel.
+EXPECTED = {SITE_FWD_P, 304}
 
 
 def test_wait_that_runs_out_reports_and_recovers():
@@ -30,7 +34,7 @@ def test_wait_that_runs_out_reports_and_recovers():
         with torch.no_grad():
             flash_naylis_attn(dev(q), dev(k), dev(v), dev(rq), dev(rk), gs.cuda(), is_causal=True)
         torch.cuda.synchronize()  # the kernel returned: no hang, no fault
-        assert lib.fna2_device_status(1) == SITE_FWD_P
+        assert lib.fna2_device_status(1) in EXPECTED
     finally:
         _lib.check(lib.fna2_debug_watchdog(0, 0), "fna2_debug_watchdog")
     # the context is intact and the next call is exact again
