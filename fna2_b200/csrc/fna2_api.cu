@@ -175,7 +175,7 @@ int map_qkv(CUtensorMap* m, const Fna2Tensor& t, const Shape& s, int rows, int h
 }
 // The backward kernels stream their non-stationary operand in tiles of
 // box_rows rows (query tiles of dkdv_query_rows rows in the key-stationary
-// kernel, 112-row key tiles in the query-stationary one) and read the streamed
+// kernel, dq_key_rows-row key tiles in the query-stationary one) and read the streamed
 // R as a 64-column SW128 atom beside it (columns past r zero-filled).
 int map_qkv_tile(CUtensorMap* m, const Fna2Tensor& t, const Shape& s, int rows, int heads, int box_rows,
                  const char* what) {
@@ -314,18 +314,19 @@ int bwd_launch(const Fna2BwdArgs* a, const Shape& s, void* scratch, void* stream
   const int qs_rows = dkdv_query_rows(s.D, s.RP);
   if (int rc = map_qkv_tile(&m.qS, a->q, s, s.rows_q(), s.H, qs_rows, "q")) return rc;
   if (int rc = map_qkv_tile(&m.dOS, a->dout, s, s.rows_q(), s.H, qs_rows, "dout")) return rc;
-  if (int rc = map_qkv_tile(&m.k112, a->k, s, s.rows_k(), s.HKV, kQT, "k")) return rc;
-  if (int rc = map_qkv_tile(&m.v112, a->v, s, s.rows_k(), s.HKV, kQT, "v")) return rc;
+  const int kd_rows = dq_key_rows(s.D, s.RP);
+  if (int rc = map_qkv_tile(&m.kDq, a->k, s, s.rows_k(), s.HKV, kd_rows, "k")) return rc;
+  if (int rc = map_qkv_tile(&m.vDq, a->v, s, s.rows_k(), s.HKV, kd_rows, "v")) return rc;
   if (s.HG > 0) {
     if (int rc = map_r(&m.rq, a->r_q, s, s.rows_q(), "r_q")) return rc;
     if (int rc = map_r(&m.rk, a->r_k, s, s.rows_k(), "r_k")) return rc;
     if (int rc = map_r_tile(&m.rqS, a->r_q, s, s.rows_q(), qs_rows, "r_q")) return rc;
-    if (int rc = map_r_tile(&m.rk112, a->r_k, s, s.rows_k(), kQT, "r_k")) return rc;
+    if (int rc = map_r_tile(&m.rkDq, a->r_k, s, s.rows_k(), kd_rows, "r_k")) return rc;
   } else {
     m.rq = m.q;  // never dereferenced: no graph heads
     m.rk = m.k;
     m.rqS = m.qS;
-    m.rk112 = m.k112;
+    m.rkDq = m.kDq;
   }
   BwdParams p;
   std::memset(&p, 0, sizeof(p));

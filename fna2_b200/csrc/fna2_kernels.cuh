@@ -19,6 +19,11 @@ constexpr float kEps = 1e-6f;  // O = acc/(l+1e-6), LSE = m + log(l+1e-6)  (flas
 // P^T fit in the 512 TMEM columns.
 __host__ __device__ constexpr int dkdv_query_rows(int D, int RP) { return (D == 128 && RP == 32) ? 64 : 96; }
 
+// Key rows per tile of the query-stationary (dQ) backward kernel: the largest
+// multiple of 16 (of 96 at most) for which [dQ | dR_q], S, dP, a separate
+// packed dS, Q and dO fit in the 512 TMEM columns.
+__host__ __device__ constexpr int dq_key_rows(int D, int RP) { return (D == 128 && RP == 32) ? 80 : 96; }
+
 // Sequence bounds of one (batch or packed sequence) index. Dense problems have
 // all sequences of length seqlen_q/seqlen_k starting at row 0 of their batch.
 struct SeqInfo {
@@ -129,7 +134,7 @@ struct BwdParams {
 struct BwdMaps {
   CUtensorMap q, k, v, dO, rq, rk;  // 128-row boxes (R with r_pad-column boxes)
   CUtensorMap qS, dOS, rqS;         // dkdv_query_rows-row boxes, streamed by the key-stationary kernel
-  CUtensorMap k112, v112, rk112;    // 112-row boxes, streamed by the query-stationary kernel
+  CUtensorMap kDq, vDq, rkDq;       // dq_key_rows-row boxes, streamed by the query-stationary kernel
 };
 
 }  // namespace fna2
