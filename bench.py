@@ -192,6 +192,122 @@ def run_reference(args, w):
 # GPU arm
 # ---------------------------------------------------------------------------
 
+def build_rows(lengths, seqs, H, D, r, dev, seed=1000):
+    """Packed inputs (q, k, v, r_q, r_k, dO) of the sequences ``seqs`` in that
+    order.  Sequence i is drawn from its own generator (seed + i), so the
+    global batch and any subset of it (a rank's shard, a check group) hold
+    identical rows: Q, K, V, dO ~ N(0, 1), R ~ N(0, 1/r), bf16."""
+    n = sum(int(lengths[i]) for i in seqs)
+    ts = [torch.empty(n, H, D, device=dev, dtype=torch.bfloat16) for _ in range(3)]
+    ts += [torch.empty(n, H, r, device=dev, dtype=torch.bfloat16) for _ in range(2)]
+    ts += [torch.empty(n, H, D, device=dev, dtype=torch.bfloat16)]
+    off = 0
+    for i in seqs:
+        L = int(lengths[i])
+        g = torch.Generator(device=dev).manual_seed(seed + i)
+        for j, t in enumerate(ts):
+            t[off:off + L].normal_(0.0, r ** -0.5 if j in (3, 4) else 1.0, generator=g)
+        off += L
+    return ts
+
+
+def scatter_batch(dist, lengths, parts, rank, world, H, D, r, dev):
+    """Rank 0 builds the seeded global batch and sends every rank its packed
+    shard over NCCL (outside the timed region); returns this rank's shard."""
+    if world == 1:
+        return build_rows(lengths, parts[0], H, D, r, dev)
+    n_me = sum(int(lengths[i]) for i in parts[rank])
+    if rank == 0:
+        glob = build_rows(lengths, range(len(lengths)), H, D, r, dev)
+        for dst in range(1, world):
+            idx = torch.tensor(PT.shard_token_index(lengths, parts[dst]), dtype=torch.long, device=dev)
+            for t in glob:
+                stage = t.index_select(0, idx)
+                dist.send(stage, dst)
+                del stage
+        idx = torch.tensor(PT.shard_token_index(lengths, parts[0]), dtype=torch.long, device=dev)
+        mine = [t.index_select(0, idx) for t in glob]
+        del glob
+        torch.cuda.empty_cache()
+        return mine
+    mine = [torch.empty((n_me, H, X), device=dev, dtype=torch.bfloat16) for X in (D, D, D, r, r, D)]
+    for t in mine:
+        dist.recv(t, 0)
+    return mine
+
+
+def check_sharding(dist, results, dgs_local, lengths, parts, rank, world, H, D, r, dev, scale, n_groups=16):
+    """Gather every rank's O and gradients to rank 0, group by group of
+    sequences in the global packing, and compare them with one GPU's result
+    for the same rows: the group recomputed on rank 0 from the seeded global
+    batch.  Per-sequence tensors must agree bit for bit (a sequence's tiles
+    do not depend on where it is packed); the all-reduced d_graph_scale must
+    equal the single-GPU sum up to fp32 summation order."""
+    from fna2_b200.flash_naylis_attn import _fna2_backward, _fna2_forward
+    own = PT.owner_of(parts)
+    cu = PT.cu_seqlens(lengths)
+    widths = [D, D, D, D, r, r]  # out, dq, dk, dv, dr_q, dr_k
+    dgs_all = dgs_local.clone()
+    if world > 1:
+        dist.all_reduce(dgs_all)
+    dgs_ref = torch.zeros(H, dtype=torch.float64, device=dev)
+    bitwise, worst = True, 0.0
+    for a, b in PT.sequence_groups(lengths, n_groups):
+        seqs = list(range(a, b))
+        mine = [i for i in seqs if own[i] == rank]
+        if rank != 0:
+            if mine:
+                rows = torch.tensor(PT.local_rows_of(lengths, parts[rank], mine), dtype=torch.long, device=dev)
+                flat = torch.cat([t.index_select(0, rows).reshape(-1) for t in results])
+                dist.send(flat, 0)
+                del flat
+            continue
+        ins = build_rows(lengths, seqs, H, D, r, dev)
+        cu_g = torch.tensor([c - cu[a] for c in cu[a:b + 1]], dtype=torch.int32, device=dev)
+        msl = max(int(lengths[i]) for i in seqs)
+        gs = torch.ones(H, device=dev)
+        out, lse = _fna2_forward(*ins[:5], gs, scale, True, cu_g, cu_g, msl, msl)
+        grads = _fna2_backward(ins[5], *ins[:5], gs, out, lse, scale, True, cu_g, cu_g, msl, msl)
+        ref = [out] + list(grads[:5])
+        dgs_ref += grads[5].double()
+        got = [torch.empty_like(x) for x in ref]
+        for src in range(world):
+            rs = [i for i in seqs if own[i] == src]
+            if not rs:
+                continue
+            g_rows = torch.tensor([j for i in rs for j in range(cu[i] - cu[a], cu[i + 1] - cu[a])],
+                                  dtype=torch.long, device=dev)
+            n = g_rows.numel()
+            if src == 0:
+                loc = torch.tensor(PT.local_rows_of(lengths, parts[0], rs), dtype=torch.long, device=dev)
+                pieces = [t.index_select(0, loc) for t in results]
+            else:
+                flat = torch.empty(n * H * sum(widths), device=dev, dtype=torch.bfloat16)
+                dist.recv(flat, src)
+                pieces, o = [], 0
+                for wd in widths:
+                    pieces.append(flat[o:o + n * H * wd].view(n, H, wd))
+                    o += n * H * wd
+            for gt, pc in zip(got, pieces):
+                gt.index_copy_(0, g_rows, pc)
+        for x, y in zip(ref, got):
+            if not torch.equal(x, y):
+                bitwise = False
+                worst = max(worst, (x.float() - y.float()).abs().max().item())
+        del ins, out, lse, grads, ref, got
+    if world > 1:
+        dist.barrier()
+    res = None
+    if rank == 0:
+        rel = ((dgs_all.double() - dgs_ref).abs().max() / dgs_ref.abs().max().clamp_min(1e-30)).item()
+        res = {"ranks": world, "groups": n_groups, "per_sequence_bitwise": bitwise,
+               "max_abs_diff": worst, "d_gs_max_rel_err": rel,
+               "scatter": "rank 0 builds the seeded global batch, NCCL send/recv of each rank's packed shard",
+               "gather": "NCCL send/recv of every rank's O and gradients to rank 0 by sequence group, compared "
+                         "with rank 0's single-GPU result for the same rows; d_gs all_reduce(sum)"}
+    return res
+
+
 def run_gpu(args, w):
     import torch.distributed as dist
     from fna2_b200 import flash_naylis_attn
@@ -213,15 +329,9 @@ def run_gpu(args, w):
     cu = PT.cu_seqlens(mine)
     T = cu[-1]
     flops_all = FL.total_flops(lengths, H, H, D, r)
-    flops_mine = FL.total_flops(mine, H, H, D, r)
     scale = 1.0 / math.sqrt(D)
 
-    g = torch.Generator(device=dev).manual_seed(1000 + rank)
-    def rnd(*shape, s=1.0):
-        return (torch.randn(*shape, device=dev, generator=g, dtype=torch.float32) * s).to(torch.bfloat16)
-    q, k, v = rnd(T, H, D), rnd(T, H, D), rnd(T, H, D)
-    rq, rk = rnd(T, H, r, s=r ** -0.5), rnd(T, H, r, s=r ** -0.5)
-    do = rnd(T, H, D)
+    q, k, v, rq, rk, do = scatter_batch(dist, lengths, parts, rank, world, H, D, r, dev)
     gs = torch.ones(H, device=dev, dtype=torch.float32)
     cu_t = torch.tensor(cu, dtype=torch.int32, device=dev)
     msl = max(mine)
@@ -235,7 +345,9 @@ def run_gpu(args, w):
 
     def step(evf=None, evb=None):
         out, lse = _fna2_forward(q, k, v, rq, rk, gs, scale, True, cu_t, cu_t, msl, msl, launch_events=evf)
-        _fna2_backward(do, q, k, v, rq, rk, gs, out, lse, scale, True, cu_t, cu_t, msl, msl, launch_events=evb)
+        grads = _fna2_backward(do, q, k, v, rq, rk, gs, out, lse, scale, True, cu_t, cu_t, msl, msl,
+                               launch_events=evb)
+        return out, grads
 
     def barrier():
         if world > 1:
@@ -292,92 +404,30 @@ def run_gpu(args, w):
     try:
         with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
             tr = json.load(f)
-        per_tok = tr.get(w["name"], {}).get(dom)
+        per_tok = tr.get("per_token_head", {}).get(dom.replace("bwd_", ""))
         if per_tok is not None:
-            traffic = per_tok * T
+            traffic = per_tok * T * H
     except Exception:
         pass
+    del ev_f, ev_b
 
     # ---------------- e2e through the public API with host buffers
-    e2e = None
+    e2e, ceiling = None, None
     if not args.no_e2e:
-        del ev_f, ev_b
-        torch.cuda.synchronize()
-        host = []
-        for t in (q, k, v, rq, rk, do):  # pinned host copies, filled without a pageable intermediate
-            h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
-            h.copy_(t)
-            host.append(h)
-        h2d = sum(t.numel() * t.element_size() for t in host)
-        leaves = [q, k, v, rq, rk]   # device buffers the host inputs are copied into each step
-        dev_do = do
-        gsl = gs.clone().requires_grad_(True)
-        res_host = torch.empty(H, dtype=torch.float32).pin_memory()
-        # Sequences go through in G contiguous groups of about T/G tokens: the inputs of
-        # group g+1 cross PCIe on a copy stream while group g computes (each group's
-        # buffers are written again only after that group's compute of the previous step).
-        G = 8
-        bounds, acc_t = [0], 0
-        for i, L in enumerate(mine):
-            acc_t += L
-            if acc_t >= T * len(bounds) / G and len(bounds) < G:
-                bounds.append(i + 1)
-        if bounds[-1] != len(mine):
-            bounds.append(len(mine))
-        groups = []
-        for a, b in zip(bounds[:-1], bounds[1:]):
-            t0g, t1g = cu[a], cu[b]
-            cu_g = torch.tensor([c - t0g for c in cu[a:b + 1]], dtype=torch.int32, device=dev)
-            groups.append((t0g, t1g, cu_g, max(mine[a:b])))
-        copy_stream = torch.cuda.Stream(device=dev)
-        done = [torch.cuda.Event() for _ in groups]
-        for e in done:
-            e.record(stream)
+        e2e, ceiling = run_e2e(args, dist, world, rank, local, dev, stream, q, k, v, rq, rk, do, gs, mine, cu,
+                               H, D, r, scale, flops_all, barrier)
 
-        def e2e_step():
-            start = torch.cuda.Event()
-            start.record(stream)
-            copied = []
-            with torch.cuda.stream(copy_stream):
-                copy_stream.wait_event(start)
-                for gi, (t0g, t1g, _, _) in enumerate(groups):
-                    copy_stream.wait_event(done[gi])
-                    for dst, src in zip(leaves + [dev_do], host):
-                        dst[t0g:t1g].copy_(src[t0g:t1g], non_blocking=True)
-                    ev = torch.cuda.Event()
-                    ev.record(copy_stream)
-                    copied.append(ev)
-            gsl.grad = None
-            keep = []
-            for gi, (t0g, t1g, cu_g, msl_g) in enumerate(groups):
-                stream.wait_event(copied[gi])
-                ins = [t[t0g:t1g].detach().requires_grad_(True) for t in leaves]
-                out = flash_naylis_attn(*ins, gsl, softmax_scale=scale, is_causal=True, cu_seqlens_q=cu_g,
-                                        cu_seqlens_k=cu_g, max_seqlen_q=msl_g, max_seqlen_k=msl_g)
-                out.backward(dev_do[t0g:t1g])
-                done[gi].record(stream)
-                keep.append((ins, out))
-            res_host.copy_(gsl.grad, non_blocking=True)
-            return keep
-
-        for _ in range(W):
-            e2e_step()
-        barrier()
+    # ---------------- the shards add up: gather, compare with one GPU's result
+    check = None
+    if not args.no_check:
+        out, grads = step()
+        results = [out] + list(grads[:5])
+        dgs_local = grads[5]
+        del q, k, v, rq, rk, do
         torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(K):
-            keep = e2e_step()
-            del keep
-        e1.record(stream)
-        torch.cuda.synchronize()
-        barrier()
-        ems = torch.tensor([e0.elapsed_time(e1) / K], device=dev, dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(ems, op=dist.ReduceOp.MAX)
-        e2e = {"value": flops_all / (float(ems.item()) / 1e3) / 1e12, "unit": "TFLOP/s",
-               "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": res_host.numel() * 4 * world,
-               "ms_per_step": float(ems.item())}
+        torch.cuda.empty_cache()
+        check = check_sharding(dist, results, dgs_local, lengths, parts, rank, world, H, D, r, dev, scale)
+        del results, out, grads
 
     from fna2_b200 import _lib
     status = _lib.load().fna2_device_status(0)
@@ -400,6 +450,8 @@ def run_gpu(args, w):
                          "traffic": traffic},
             "kernels_ms": kern,
             "e2e": e2e,
+            "copy_ceiling": ceiling,
+            "sharding_check": check,
             "gpu_launches": 4 * K,
             "clocks": clk,
             "cpu_baseline": cpu,
@@ -409,6 +461,153 @@ def run_gpu(args, w):
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+
+
+def run_e2e(args, dist, world, rank, local, dev, stream, q, k, v, rq, rk, do, gs, mine, cu, H, D, r, scale,
+            flops_all, barrier):
+    """The metric through the public API (flash_naylis_attn + backward) with
+    host buffers: every step copies its inputs from pinned host memory and
+    copies O and the five gradients (and d_graph_scale) back to pinned host
+    memory.  The sequences go through in G groups on three streams, so that
+    group g+1's inputs cross PCIe to the GPU while group g computes and group
+    g-1's results cross back.  Also measures the copy ceiling of this host
+    link alone: the same bytes in, out, and in and out at once, no compute."""
+    from fna2_b200 import flash_naylis_attn
+    K, W = args.steps, args.warmup
+    T = cu[-1]
+    torch.cuda.synchronize()
+    host_in = []
+    for t in (q, k, v, rq, rk, do):  # pinned host copies, filled without a pageable intermediate
+        h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+        h.copy_(t)
+        host_in.append(h)
+    # results: O, dq, dk, dv, dr_q, dr_k (bf16) and d_graph_scale (fp32)
+    host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (q, q, k, v, rq, rk)]
+    host_dgs = torch.empty(H, dtype=torch.float32, pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = sum(t.numel() * t.element_size() for t in host_out) + host_dgs.numel() * 4
+    leaves = [q, k, v, rq, rk]   # device buffers the host inputs are copied into each step
+    gsl = gs.clone().requires_grad_(True)
+    G = 8
+    bounds, acc_t = [0], 0
+    for i, L in enumerate(mine):
+        acc_t += L
+        if acc_t >= T * len(bounds) / G and len(bounds) < G:
+            bounds.append(i + 1)
+    if bounds[-1] != len(mine):
+        bounds.append(len(mine))
+    groups = []
+    for a, b in zip(bounds[:-1], bounds[1:]):
+        t0g, t1g = cu[a], cu[b]
+        cu_g = torch.tensor([c - t0g for c in cu[a:b + 1]], dtype=torch.int32, device=dev)
+        groups.append((t0g, t1g, cu_g, max(mine[a:b])))
+    copy_in = torch.cuda.Stream(device=dev)
+    copy_out = torch.cuda.Stream(device=dev)
+    done = [torch.cuda.Event() for _ in groups]
+    for e in done:
+        e.record(stream)
+
+    def e2e_step():
+        start = torch.cuda.Event()
+        start.record(stream)
+        copied = []
+        with torch.cuda.stream(copy_in):
+            copy_in.wait_event(start)
+            for gi, (t0g, t1g, _, _) in enumerate(groups):
+                copy_in.wait_event(done[gi])  # group gi's previous compute has read these buffers
+                for dst, src in zip(leaves + [do], host_in):
+                    dst[t0g:t1g].copy_(src[t0g:t1g], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(copy_in)
+                copied.append(ev)
+        gsl.grad = None
+        keep = []
+        for gi, (t0g, t1g, cu_g, msl_g) in enumerate(groups):
+            stream.wait_event(copied[gi])
+            ins = [t[t0g:t1g].detach().requires_grad_(True) for t in leaves]
+            out = flash_naylis_attn(*ins, gsl, softmax_scale=scale, is_causal=True, cu_seqlens_q=cu_g,
+                                    cu_seqlens_k=cu_g, max_seqlen_q=msl_g, max_seqlen_k=msl_g)
+            out.backward(do[t0g:t1g])
+            done[gi].record(stream)
+            res = [out.detach()] + [x.grad for x in ins]
+            with torch.cuda.stream(copy_out):
+                copy_out.wait_event(done[gi])
+                for dst, src in zip(host_out, res):
+                    dst[t0g:t1g].copy_(src, non_blocking=True)
+            keep.append(res)
+        finish = torch.cuda.Event()
+        with torch.cuda.stream(copy_out):
+            copy_out.wait_event(done[-1])  # d_graph_scale is complete after the last group
+            host_dgs.copy_(gsl.grad, non_blocking=True)
+            finish.record(copy_out)
+        stream.wait_event(finish)  # the step ends when its results are on the host
+        return keep
+
+    def timed(fn, n):
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            keep = fn()
+            del keep
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        t = torch.tensor([e0.elapsed_time(e1) / n], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(W):
+        del_keep = e2e_step()
+        del del_keep
+    ems = timed(e2e_step, K)
+    e2e = {"value": flops_all / (ems / 1e3) / 1e12, "unit": "TFLOP/s",
+           "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world, "ms_per_step": ems}
+
+    # copy ceiling of the host link: the same bytes, the same group copies, no compute
+    dev_out = [torch.empty_like(t) for t in host_out]
+
+    def copies(inp, outp):
+        def fn():
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            ends = []
+            if inp:
+                with torch.cuda.stream(copy_in):
+                    copy_in.wait_event(ev)
+                    for t0g, t1g, _, _ in groups:
+                        for dst, src in zip(leaves + [do], host_in):
+                            dst[t0g:t1g].copy_(src[t0g:t1g], non_blocking=True)
+                    e = torch.cuda.Event()
+                    e.record(copy_in)
+                    ends.append(e)
+            if outp:
+                with torch.cuda.stream(copy_out):
+                    copy_out.wait_event(ev)
+                    for t0g, t1g, _, _ in groups:
+                        for dst, src in zip(host_out, dev_out):
+                            dst[t0g:t1g].copy_(src[t0g:t1g], non_blocking=True)
+                    e = torch.cuda.Event()
+                    e.record(copy_out)
+                    ends.append(e)
+            for e in ends:
+                stream.wait_event(e)
+            return None
+        return fn
+
+    n_c = max(1, min(K, 3))
+    ms_in = timed(copies(True, False), n_c)
+    ms_out = timed(copies(False, True), n_c)
+    ms_both = timed(copies(True, True), n_c)
+    ceiling = {"h2d_gbs_per_gpu": h2d / (ms_in / 1e3) / 1e9, "d2h_gbs_per_gpu": d2h / (ms_out / 1e3) / 1e9,
+               "both_ms_per_step": ms_both, "both_gbs_per_gpu": (h2d + d2h) / (ms_both / 1e3) / 1e9,
+               "e2e_over_ceiling_ms": ems / ms_both,
+               "note": "same bytes and group copies as e2e, without compute; max over ranks"}
+    e2e["copy_ceiling_fraction"] = ms_both / ems
+    del dev_out, host_in, host_out
+    return e2e, ceiling
 
 
 def run_qk_prep(args, w):
@@ -652,6 +851,7 @@ def main():
     ap.add_argument("--workload", default="cfg5", choices=["cfg5", "cfg3", "cfg2", "cfg4"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-check", action="store_true", help="skip the gather-and-compare check of the shards")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--op", default="attention", choices=["attention", "qk_prep", "decode", "rel_proj"])
     args = ap.parse_args()

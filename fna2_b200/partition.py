@@ -4,13 +4,17 @@ Units are whole sequences (all heads of a sequence stay on one rank, so GQA
 groups never split and dK/dV need no cross-GPU reduction).  A unit's cost is
 its causal fwd+bwd FLOPs, proportional to L^2.  Longest-processing-time
 greedy: sort by cost descending, give each unit to the least loaded rank.
+
+Also the row maps of the multi-GPU data plane: which rows of the global
+packed batch a rank owns (scatter), where its results go back (gather), and
+the contiguous sequence groups in which rank 0 re-checks the gathered results.
 """
 from __future__ import annotations
 
 import heapq
 import math
 import random
-from typing import List, Sequence
+from typing import List, Sequence, Tuple
 
 
 def lpt_partition(lengths: Sequence[int], world: int) -> List[List[int]]:
@@ -81,3 +85,40 @@ def gather_rows(local_tensors, lengths: Sequence[int], parts: List[List[int]]):
         idx = torch.tensor(shard_token_index(lengths, parts[rank]), dtype=torch.long, device=t.device)
         out.index_copy_(0, idx, t)
     return out
+
+
+def local_rows_of(lengths: Sequence[int], part: Sequence[int], seqs: Sequence[int]) -> List[int]:
+    """Rows, in a rank's local packing (its sequences ``part`` in order), of the
+    sequences ``seqs`` (a subset of ``part``, in the order given)."""
+    pos = {}
+    off = 0
+    for i in part:
+        pos[i] = off
+        off += int(lengths[i])
+    rows: List[int] = []
+    for i in seqs:
+        rows.extend(range(pos[i], pos[i] + int(lengths[i])))
+    return rows
+
+
+def sequence_groups(lengths: Sequence[int], n_groups: int) -> List[Tuple[int, int]]:
+    """Split the sequences (in global order) into at most ``n_groups``
+    contiguous ranges [a, b) of about equal token counts."""
+    T = sum(int(L) for L in lengths)
+    bounds, acc = [0], 0
+    for i, L in enumerate(lengths):
+        acc += int(L)
+        if acc >= T * len(bounds) / n_groups and len(bounds) < n_groups and i + 1 < len(lengths):
+            bounds.append(i + 1)
+    bounds.append(len(lengths))
+    return [(a, b) for a, b in zip(bounds[:-1], bounds[1:]) if b > a]
+
+
+def owner_of(parts: List[List[int]]) -> List[int]:
+    """Rank owning each sequence."""
+    n = sum(len(p) for p in parts)
+    own = [-1] * n
+    for r, p in enumerate(parts):
+        for i in p:
+            own[i] = r
+    return own

@@ -95,11 +95,21 @@ def attention_fwd(q, k, v, r_q, r_k, gs, scale: float, causal: bool = True):
     return out, lse
 
 
-def attention_bwd(q, k, v, r_q, r_k, gs, out, lse, dout, scale: float, causal: bool = True):
+def attention_bwd(q, k, v, r_q, r_k, gs, out, lse, dout, scale: float, causal: bool = True,
+                  ds_bf16: bool = False, dgs_terms: bool = False):
     """Explicit FA2-style backward (flash_naylis_attn.py:356-693).
 
     Returns (dq, dk, dv, dr_q, dr_k, d_gs); dk/dv are summed over the query
     heads that share a KV head (the reference's atomic_add, :546-547).
+
+    ``ds_bf16`` rounds dS to bf16 before every contraction that consumes it
+    (dq, dk, dr_q, dr_k and d_gs): the arithmetic of the sm_100a kernels,
+    which feed dS to the tensor cores in bf16 and form d_gs from the same
+    contraction.  The reference rounds dS to bf16 for dq/dk/dr (``ds.to(
+    q.dtype)``, :529,:535,:679,:683) but sums d_gs from the fp32 dS (:537-538).
+    ``dgs_terms`` appends, per graph head, the sum of squares of the d_gs
+    summands dS_ij * (R_q R_k^T)_ij (its conditioning: rounding each summand
+    by a relative eps moves the sum by about eps times its square root).
     """
     b, h, s_q, d = q.shape
     hkv = k.shape[1]
@@ -113,6 +123,8 @@ def attention_bwd(q, k, v, r_q, r_k, gs, out, lse, dout, scale: float, causal: b
     ke = _expand_kv(k, h)
     dp = torch.einsum("bhid,bhjd->bhij", dout, ve)                 # :522
     ds = p * (dp - delta)                                          # :523
+    if ds_bf16:
+        ds = ds.to(torch.bfloat16).to(ds.dtype)
     dv_e = torch.einsum("bhij,bhid->bhjd", p, dout)                # :527
     dk_e = scale * torch.einsum("bhij,bhid->bhjd", ds, q)          # :529
     dq = scale * torch.einsum("bhij,bhjd->bhid", ds, ke)           # :679
@@ -124,6 +136,8 @@ def attention_bwd(q, k, v, r_q, r_k, gs, out, lse, dout, scale: float, causal: b
     dr_k = gsv * torch.einsum("bhij,bhir->bhjr", dsg, r_q)         # :535
     raw = torch.einsum("bhir,bhjr->bhij", r_q, r_k)
     d_gs = (dsg * raw).sum(dim=(0, 2, 3))                          # :537-538,553
+    if dgs_terms:
+        return dq, dk, dv, dr_q, dr_k, d_gs, (dsg * raw).square().sum(dim=(0, 2, 3))
     return dq, dk, dv, dr_q, dr_k, d_gs
 
 
@@ -177,11 +191,14 @@ def varlen_fwd(q, k, v, r_q, r_k, gs, cu_q: Sequence[int], cu_k: Sequence[int], 
     return out, lse
 
 
-def varlen_bwd(q, k, v, r_q, r_k, gs, out, lse, dout, cu_q, cu_k, scale: float):
-    """Packed backward: per-sequence explicit backward, concatenated, d_gs summed."""
+def varlen_bwd(q, k, v, r_q, r_k, gs, out, lse, dout, cu_q, cu_k, scale: float, ds_bf16: bool = False,
+               dgs_terms: bool = False):
+    """Packed backward: per-sequence explicit backward, concatenated, d_gs summed
+    (with ``dgs_terms``, the summed squares of the d_gs summands appended)."""
     dq, dk, dv = torch.zeros_like(q), torch.zeros_like(k), torch.zeros_like(v)
     drq, drk = torch.zeros_like(r_q), torch.zeros_like(r_k)
     dgs = torch.zeros_like(gs, dtype=q.dtype)
+    terms = torch.zeros_like(gs, dtype=q.dtype)
     for i in range(len(cu_q) - 1):
         a, b = int(cu_q[i]), int(cu_q[i + 1])
         c, d = int(cu_k[i]), int(cu_k[i + 1])
@@ -190,13 +207,17 @@ def varlen_bwd(q, k, v, r_q, r_k, gs, out, lse, dout, cu_q, cu_k, scale: float):
         g = attention_bwd(_seq_view(q, a, b), _seq_view(k, c, d), _seq_view(v, c, d),
                           _seq_view(r_q, a, b), _seq_view(r_k, c, d), gs,
                           _seq_view(out, a, b), lse[a:b].transpose(0, 1).unsqueeze(0),
-                          _seq_view(dout, a, b), scale, True)
+                          _seq_view(dout, a, b), scale, True, ds_bf16, dgs_terms)
         dq[a:b] = g[0][0].transpose(0, 1)
         dk[c:d] += g[1][0].transpose(0, 1)
         dv[c:d] += g[2][0].transpose(0, 1)
         drq[a:b] = g[3][0].transpose(0, 1)
         drk[c:d] += g[4][0].transpose(0, 1)
         dgs += g[5]
+        if dgs_terms:
+            terms += g[6]
+    if dgs_terms:
+        return dq, dk, dv, drq, drk, dgs, terms
     return dq, dk, dv, drq, drk, dgs
 
 

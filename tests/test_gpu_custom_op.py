@@ -66,5 +66,9 @@ def test_compiled_module_matches_eager(mode):
     eager = run(f)
     torch._dynamo.reset()
     compiled = run(torch.compile(f, fullgraph=True))
-    for a, b in zip(eager, compiled):
-        assert torch.equal(a, b)
+    names = ("out", "dq", "dk", "dv", "drq", "drk", "dgs")
+    for n, a, b in zip(names, eager, compiled):
+        if n == "dgs":  # summed with fp32 atomics: equal up to summation order
+            torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-5)
+        else:
+            assert torch.equal(a, b), n
