@@ -77,6 +77,16 @@ def workload(name: str):
     if name == "cfg4":
         return dict(name="cfg4", lengths=[32768], H=32, D=128, r=32,
                     desc="BASELINE config 4: one sequence of 32768, H32 D128 r32")
+    if name == "cfg5short":
+        lengths = [L for L in PT.loguniform_lengths(512, 128, 16384, seed=0) if L <= 512]
+        return dict(name="cfg5short", lengths=lengths, H=32, D=128, r=16,
+                    desc=f"BASELINE config 5's sequences with L <= 512 ({len(lengths)} seqs): the short-sequence "
+                         "regime, H32 D128 r16")
+    if name.startswith("seqs:"):
+        # seqs:N:L:H:r -- N packed sequences of L tokens (profiling and small cases)
+        n, L, H, r = (int(x) for x in name.split(":")[1:])
+        return dict(name=name, lengths=[L] * n, H=H, D=128, r=r,
+                    desc=f"{n} packed sequences of {L}, H{H} D128 r{r}, causal bf16, gs=1")
     raise ValueError(name)
 
 
@@ -204,7 +214,7 @@ def build_rows(lengths, seqs, H, D, r, dev, seed=1000):
     off = 0
     for i in seqs:
         L = int(lengths[i])
-        g = torch.Generator(device=dev).manual_seed(seed + i)
+        g = torch.Generator(device=torch.device(dev).type).manual_seed(seed + i)
         for j, t in enumerate(ts):
             t[off:off + L].normal_(0.0, r ** -0.5 if j in (3, 4) else 1.0, generator=g)
         off += L
@@ -236,14 +246,23 @@ def scatter_batch(dist, lengths, parts, rank, world, H, D, r, dev):
     return mine
 
 
-def check_sharding(dist, results, dgs_local, lengths, parts, rank, world, H, D, r, dev, scale, n_groups=16):
+def cuda_fwd_bwd(ins, cu_g, msl, scale):
+    """Forward + backward of one packed batch through the library's launchers:
+    (out, dq, dk, dv, dr_q, dr_k, d_gs)."""
+    from fna2_b200.flash_naylis_attn import _fna2_backward, _fna2_forward
+    gs = torch.ones(ins[0].shape[1], device=ins[0].device)
+    out, lse = _fna2_forward(*ins[:5], gs, scale, True, cu_g, cu_g, msl, msl)
+    return (out,) + tuple(_fna2_backward(ins[5], *ins[:5], gs, out, lse, scale, True, cu_g, cu_g, msl, msl))
+
+
+def check_sharding(dist, results, dgs_local, lengths, parts, rank, world, H, D, r, dev, scale, n_groups=16,
+                   compute=cuda_fwd_bwd):
     """Gather every rank's O and gradients to rank 0, group by group of
     sequences in the global packing, and compare them with one GPU's result
     for the same rows: the group recomputed on rank 0 from the seeded global
-    batch.  Per-sequence tensors must agree bit for bit (a sequence's tiles
-    do not depend on where it is packed); the all-reduced d_graph_scale must
-    equal the single-GPU sum up to fp32 summation order."""
-    from fna2_b200.flash_naylis_attn import _fna2_backward, _fna2_forward
+    batch (``compute``).  Per-sequence tensors must agree bit for bit (a
+    sequence's tiles do not depend on where it is packed); the all-reduced
+    d_graph_scale must equal the single-GPU sum up to fp32 summation order."""
     own = PT.owner_of(parts)
     cu = PT.cu_seqlens(lengths)
     widths = [D, D, D, D, r, r]  # out, dq, dk, dv, dr_q, dr_k
@@ -265,11 +284,9 @@ def check_sharding(dist, results, dgs_local, lengths, parts, rank, world, H, D, 
         ins = build_rows(lengths, seqs, H, D, r, dev)
         cu_g = torch.tensor([c - cu[a] for c in cu[a:b + 1]], dtype=torch.int32, device=dev)
         msl = max(int(lengths[i]) for i in seqs)
-        gs = torch.ones(H, device=dev)
-        out, lse = _fna2_forward(*ins[:5], gs, scale, True, cu_g, cu_g, msl, msl)
-        grads = _fna2_backward(ins[5], *ins[:5], gs, out, lse, scale, True, cu_g, cu_g, msl, msl)
-        ref = [out] + list(grads[:5])
-        dgs_ref += grads[5].double()
+        res_g = compute(ins, cu_g, msl, scale)
+        ref = list(res_g[:6])
+        dgs_ref += res_g[6].double()
         got = [torch.empty_like(x) for x in ref]
         for src in range(world):
             rs = [i for i in seqs if own[i] == src]
@@ -294,7 +311,7 @@ def check_sharding(dist, results, dgs_local, lengths, parts, rank, world, H, D, 
             if not torch.equal(x, y):
                 bitwise = False
                 worst = max(worst, (x.float() - y.float()).abs().max().item())
-        del ins, out, lse, grads, ref, got
+        del ins, res_g, ref, got
     if world > 1:
         dist.barrier()
     res = None
@@ -476,14 +493,31 @@ def run_e2e(args, dist, world, rank, local, dev, stream, q, k, v, rq, rk, do, gs
     K, W = args.steps, args.warmup
     T = cu[-1]
     torch.cuda.synchronize()
-    host_in = []
-    for t in (q, k, v, rq, rk, do):  # pinned host copies, filled without a pageable intermediate
-        h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+    # inputs (q, k, v, r_q, r_k, dO) and results (O, dq, dk, dv, dr_q, dr_k) in
+    # page-locked host memory: one exact-size buffer per direction, registered
+    # with cudaHostRegister (PyTorch's pinned allocator rounds every tensor up
+    # to a power of two, ~10 GB more at config 5)
+    pinned = []
+
+    def host_tensors(like):
+        nbytes = [t.numel() * t.element_size() for t in like]
+        buf = torch.empty(sum(nbytes), dtype=torch.uint8)
+        rc = torch.cuda.cudart().cudaHostRegister(buf.data_ptr(), buf.numel(), 0)
+        if int(rc) != 0:
+            raise RuntimeError(f"cudaHostRegister of {buf.numel()} bytes failed ({rc})")
+        pinned.append(buf)
+        views, off = [], 0
+        for t, nb in zip(like, nbytes):
+            views.append(buf[off:off + nb].view(t.dtype).view(t.shape))
+            off += nb
+        return views
+
+    host_in = host_tensors([q, k, v, rq, rk, do])
+    for h, t in zip(host_in, (q, k, v, rq, rk, do)):
         h.copy_(t)
-        host_in.append(h)
-    # results: O, dq, dk, dv, dr_q, dr_k (bf16) and d_graph_scale (fp32)
-    host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (q, q, k, v, rq, rk)]
+    host_out = host_tensors([q, q, k, v, rq, rk])  # O, dq, dk, dv, dr_q, dr_k
     host_dgs = torch.empty(H, dtype=torch.float32, pin_memory=True)
+    assert all(t.is_pinned() for t in host_in + host_out)
     h2d = sum(t.numel() * t.element_size() for t in host_in)
     d2h = sum(t.numel() * t.element_size() for t in host_out) + host_dgs.numel() * 4
     leaves = [q, k, v, rq, rk]   # device buffers the host inputs are copied into each step
@@ -606,7 +640,10 @@ def run_e2e(args, dist, world, rank, local, dev, stream, q, k, v, rq, rk, do, gs
                "e2e_over_ceiling_ms": ems / ms_both,
                "note": "same bytes and group copies as e2e, without compute; max over ranks"}
     e2e["copy_ceiling_fraction"] = ms_both / ems
+    torch.cuda.synchronize()
     del dev_out, host_in, host_out
+    for buf in pinned:
+        torch.cuda.cudart().cudaHostUnregister(buf.data_ptr())
     return e2e, ceiling
 
 
@@ -848,7 +885,8 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="fna2", choices=["fna2", "reference"])
-    ap.add_argument("--workload", default="cfg5", choices=["cfg5", "cfg3", "cfg2", "cfg4"])
+    ap.add_argument("--workload", default="cfg5",
+                    help="cfg5 (default), cfg3, cfg2, cfg4, cfg5short, or seqs:N:L:H:r")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-check", action="store_true", help="skip the gather-and-compare check of the shards")

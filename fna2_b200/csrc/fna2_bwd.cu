@@ -420,17 +420,18 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
   float* vec = reinterpret_cast<float*>(smem + L::oVec);
 
   const ProblemDev& P = p.prob;
-  const int hk = blockIdx.y;
-  int n_blk;
+  int n_blk, hk;
   SeqInfo si;
-  if (P.varlen) {  // one CTA per real key tile (table written by the pre kernel)
+  if (P.varlen) {  // grid (table entry, KV head): one CTA per real key tile (table from the pre kernel)
+    hk = blockIdx.y;
     const int4 e0 = p.tab_k[2 * blockIdx.x], e1 = p.tab_k[2 * blockIdx.x + 1];
     if (e0.x < 0) return;
     n_blk = e0.x;
     si.q_start = e0.y, si.k_start = e0.z, si.len_q = e0.w, si.len_k = e1.x, si.b = 0;
-  } else {
-    n_blk = blockIdx.x;
-    si = seq_info(P, blockIdx.z);
+  } else {  // grid (KV head, batch, key tile): key tile 0, the heaviest causal one, launches first
+    hk = blockIdx.x;
+    n_blk = blockIdx.z;
+    si = seq_info(P, blockIdx.y);
   }
   const int n0 = n_blk * kBlockN;
   if (n0 >= si.len_k) return;
@@ -943,17 +944,18 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::oMisc + 4);
 
   const ProblemDev& P = p.prob;
-  const int h = blockIdx.y;
-  int m_blk;
+  int m_blk, h;
   SeqInfo si;
-  if (P.varlen) {  // one CTA per real query tile (table written by the pre kernel)
+  if (P.varlen) {  // grid (table entry, head): one CTA per real query tile (table from the pre kernel)
+    h = blockIdx.y;
     const int4 e0 = p.tab_q[2 * blockIdx.x], e1 = p.tab_q[2 * blockIdx.x + 1];
     if (e0.x < 0) return;
     m_blk = e0.x;
     si.q_start = e0.y, si.k_start = e0.z, si.len_q = e0.w, si.len_k = e1.x, si.b = 0;
-  } else {
-    m_blk = p.n_mblocks - 1 - static_cast<int>(blockIdx.x);
-    si = seq_info(P, blockIdx.z);
+  } else {  // grid (head, batch, query tile): the last, heaviest causal tile launches first
+    h = blockIdx.x;
+    m_blk = p.n_mblocks - 1 - static_cast<int>(blockIdx.z);
+    si = seq_info(P, blockIdx.y);
   }
   const int q0 = m_blk * kBlockM;
   if (q0 >= si.len_q) return;
@@ -1322,7 +1324,7 @@ cudaError_t launch_bwd_t(const BwdMaps& m, const BwdParams& p, cudaStream_t stre
     auto kern = fna2_bwd_dkdv_kernel<D, RP>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
     if (e != cudaSuccess) return e;
-    dim3 grid(p.prob.varlen ? p.tab_k_len : p.n_nblocks, p.prob.heads_kv, p.prob.varlen ? 1 : p.batch);
+    const dim3 grid = p.prob.varlen ? dim3(p.tab_k_len, p.prob.heads_kv, 1) : dim3(p.prob.heads_kv, p.batch, p.n_nblocks);
     kern<<<grid, kDkdvThreads, L::kTotal, stream>>>(m.qS, m.k, m.v, m.dOS, m.rqS, m.rk, p);
     e = cudaGetLastError();
     if (e == cudaSuccess && ev) e = cudaEventRecord(ev[2], stream);
@@ -1333,7 +1335,7 @@ cudaError_t launch_bwd_t(const BwdMaps& m, const BwdParams& p, cudaStream_t stre
     auto kern = fna2_bwd_dq_kernel<D, RP>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
     if (e != cudaSuccess) return e;
-    dim3 grid(p.prob.varlen ? p.tab_q_len : p.n_mblocks, p.prob.heads, p.prob.varlen ? 1 : p.batch);
+    const dim3 grid = p.prob.varlen ? dim3(p.tab_q_len, p.prob.heads, 1) : dim3(p.prob.heads, p.batch, p.n_mblocks);
     kern<<<grid, kDqThreads, L::kTotal, stream>>>(m.q, m.kDq, m.vDq, m.dO, m.rq, m.rkDq, p);
     e = cudaGetLastError();
     if (e == cudaSuccess && ev) e = cudaEventRecord(ev[3], stream);

@@ -78,3 +78,62 @@ def test_two_gloo_ranks_reassemble_the_single_process_result():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert q.get(timeout=5) is True
+
+
+def _oracle_fwd_bwd(ins, cu_g, msl, scale):
+    """The CPU oracle in the role of one GPU's fwd + bwd, with the kernels'
+    output dtypes (bf16 tensors, fp32 d_gs)."""
+    from oracle import fna2_oracle as O
+    cu = cu_g.tolist()
+    q, k, v, rq, rk, do = (t.double() for t in ins)
+    gs = torch.ones(q.shape[1], dtype=torch.float64)
+    out, lse = O.varlen_fwd(q, k, v, rq, rk, gs, cu, cu, scale)
+    g = O.varlen_bwd(q, k, v, rq, rk, gs, out, lse, do, cu, cu, scale)
+    return tuple(t.to(torch.bfloat16) for t in (out,) + g[:5]) + (g[5].float(),)
+
+
+def _dataplane_worker(rank, world, port, q, plant):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import bench
+        L = [17, 3, 40, 9, 25, 1, 12]
+        H, D, r = 2, 16, 8
+        parts = PT.lpt_partition(L, world)
+        mine = [L[i] for i in parts[rank]]
+        shard = bench.scatter_batch(dist, L, parts, rank, world, H, D, r, "cpu")
+        # the shard is exactly the global batch's rows of this rank's sequences
+        assert all(torch.equal(a, b) for a, b in zip(shard, bench.build_rows(L, parts[rank], H, D, r, "cpu")))
+        cu_l = torch.tensor(PT.cu_seqlens(mine), dtype=torch.int32)
+        res = _oracle_fwd_bwd(shard, cu_l, max(mine), 0.25)
+        results = list(res[:6])
+        if plant and rank == 1:  # a mistake planted in one rank's result must be caught
+            results[2] = results[2].clone()
+            results[2][0, 0, 0] += 1.0
+        chk = bench.check_sharding(dist, results, res[6], L, parts, rank, world, H, D, r, "cpu", 0.25, n_groups=3,
+                                   compute=_oracle_fwd_bwd)
+        if rank == 0:
+            q.put(chk)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("plant", [False, True])
+def test_bench_dataplane_scatter_gather_check(plant):
+    """bench.py's multi-GPU data plane on two gloo ranks: rank 0 builds the
+    seeded global batch and sends each rank its shard; the gathered results
+    equal one process's results for the global packing bit for bit, and
+    d_gs's all-reduce equals the single-process sum; a planted mistake is
+    reported."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29600 + os.getpid() % 1000 + (7 if plant else 0)
+    procs = [ctx.Process(target=_dataplane_worker, args=(r, 2, port, q, plant)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+        assert p.exitcode == 0
+    chk = q.get(timeout=5)
+    assert chk["per_sequence_bitwise"] is (not plant), chk
+    assert chk["d_gs_max_rel_err"] < 1e-5, chk
