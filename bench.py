@@ -597,8 +597,12 @@ def run_e2e(args, dist, world, rank, local, dev, stream, q, k, v, rq, rk, do, gs
         del_keep = e2e_step()
         del del_keep
     ems = timed(e2e_step, K)
+    nbytes = torch.tensor([h2d, d2h], device=dev, dtype=torch.float64)
+    if world > 1:  # every rank copies its own shard: sum the bytes
+        dist.all_reduce(nbytes)
+    h2d_all, d2h_all = int(nbytes[0].item()), int(nbytes[1].item())
     e2e = {"value": flops_all / (ems / 1e3) / 1e12, "unit": "TFLOP/s",
-           "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world, "ms_per_step": ems}
+           "h2d_bytes_per_step": h2d_all, "d2h_bytes_per_step": d2h_all, "ms_per_step": ems}
 
     # copy ceiling of the host link: the same bytes, the same group copies, no compute
     dev_out = [torch.empty_like(t) for t in host_out]
@@ -635,10 +639,11 @@ def run_e2e(args, dist, world, rank, local, dev, stream, q, k, v, rq, rk, do, gs
     ms_in = timed(copies(True, False), n_c)
     ms_out = timed(copies(False, True), n_c)
     ms_both = timed(copies(True, True), n_c)
-    ceiling = {"h2d_gbs_per_gpu": h2d / (ms_in / 1e3) / 1e9, "d2h_gbs_per_gpu": d2h / (ms_out / 1e3) / 1e9,
-               "both_ms_per_step": ms_both, "both_gbs_per_gpu": (h2d + d2h) / (ms_both / 1e3) / 1e9,
+    ceiling = {"h2d_gbs": h2d_all / (ms_in / 1e3) / 1e9, "d2h_gbs": d2h_all / (ms_out / 1e3) / 1e9,
+               "both_ms_per_step": ms_both, "both_gbs": (h2d_all + d2h_all) / (ms_both / 1e3) / 1e9,
                "e2e_over_ceiling_ms": ems / ms_both,
-               "note": "same bytes and group copies as e2e, without compute; max over ranks"}
+               "note": "the same bytes and group copies as e2e without compute, all ranks together "
+                       "(time = max over ranks): the host link's ceiling for e2e"}
     e2e["copy_ceiling_fraction"] = ms_both / ems
     torch.cuda.synchronize()
     del dev_out, host_in, host_out

@@ -143,8 +143,6 @@ int check_problem(const Fna2Problem& p, Shape* s) {
   s->r = p.heads_graph > 0 ? p.rank : 16;
   s->RP = s->r <= 16 ? 16 : 32;
   if (!s->varlen) FNA2_CHECK(p.seqlen_q == p.seqlen_k, "dense problems need seqlen_q == seqlen_k");
-  // grid z counts query-tile pairs / tiles (at most 65535)
-  FNA2_CHECK(p.seqlen_q <= 65535 * 128 && p.seqlen_k <= 65535 * 128, "sequence lengths must be <= %d", 65535 * 128);
   return FNA2_OK;
 }
 

@@ -420,18 +420,17 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
   float* vec = reinterpret_cast<float*>(smem + L::oVec);
 
   const ProblemDev& P = p.prob;
-  int n_blk, hk;
+  const int hk = blockIdx.y;
+  int n_blk;
   SeqInfo si;
-  if (P.varlen) {  // grid (table entry, KV head): one CTA per real key tile (table from the pre kernel)
-    hk = blockIdx.y;
+  if (P.varlen) {  // one CTA per real key tile (table written by the pre kernel)
     const int4 e0 = p.tab_k[2 * blockIdx.x], e1 = p.tab_k[2 * blockIdx.x + 1];
     if (e0.x < 0) return;
     n_blk = e0.x;
     si.q_start = e0.y, si.k_start = e0.z, si.len_q = e0.w, si.len_k = e1.x, si.b = 0;
-  } else {  // grid (KV head, batch, key tile): key tile 0, the heaviest causal one, launches first
-    hk = blockIdx.x;
-    n_blk = blockIdx.z;
-    si = seq_info(P, blockIdx.y);
+  } else {
+    n_blk = blockIdx.x;
+    si = seq_info(P, blockIdx.z);
   }
   const int n0 = n_blk * kBlockN;
   if (n0 >= si.len_k) return;
@@ -825,52 +824,39 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
   }
 }
 
+constexpr int kQT = dq_key_rows(128, 16);  // key rows per tile of the query-stationary (dQ) kernel
+
 // ---------------------------------------------------------------------------
 // dQ / dR_q / d_gs  (Q-stationary)
 // ---------------------------------------------------------------------------
 // One CTA per (128-row query tile, head, sequence), looping over the causally
-// visible key tiles of KT rows (dq_key_rows: 96, or 80 for head_dim 128 with
-// r_pad 32).  The stationary Q and dO tiles live in tensor memory (A operands
-// of the S and dP MMAs in the TS form), which leaves shared memory for
-// three-deep K and V rings.  They arrive by TMA in the V ring (before its
-// first use) and are moved to tensor memory by tcgen05.cp.
+// visible 112-row key tiles.  The stationary Q and dO tiles live in tensor
+// memory (A operands of the S and dP MMAs in the TS form), which leaves shared
+// memory for three-deep K and V rings.  They arrive by TMA in the V ring
+// (before its first use) and are moved to tensor memory by tcgen05.cp.
 // dR_q rides along with dQ as extra accumulator columns: the B operand of the
 // dQ MMA is [K | R_k] (R_k as a zero-padded third 64-column swizzle atom next
 // to K's two), so one N = D + r_pad MMA per k-step yields dQ and dS R_k
 // together.
-// TMEM columns: [dQ | dS R_k] (D + r_pad) | S (KT) | dP (KT) | dS (KT/2,
-// packed bf16) | Q (D/2) | dO (D/2).  dS has columns of its own, so the next
-// tile's dP is computed as soon as the warps have read this tile's dP, while
-// they form dS and the tensor core runs the previous dQ: per tile the tensor
-// core sees S(j+1), dP(j+1), dQ(j) back to back.
+// TMEM columns: [dQ | dS R_k] [0,160) S [160,272) dP [272,384) Q [384,448)
+// dO [448,512).
 // Key tiles are visited from the diagonal down to the first one: the CTAs of
 // one head then read different tiles at any moment, so each tile comes from
 // HBM once and from L2 for the other CTAs, instead of all of them waiting on
 // the same misses in lockstep.
-// Per key tile (warpgroup w owns keys [w*KT/2, (w+1)*KT/2); thread = query
-// row = TMEM lane):
+// Per key tile (112 columns; warpgroup 0 owns [0,64), warpgroup 1 [64,112);
+// thread = query row = TMEM lane):
 //   S = Q K^T (+ R~_q R_k^T) -> warps: P = exp2(S*c - LSE2) in registers
 //   dP = dO V^T              -> warps: dS = P (dP - Delta) as bf16 into the
-//                               dS columns (once dQ of the previous tile has
-//                               read them)
+//                               first half of their own dP columns
 //   [dQ | dS R_k] += dS [K | R_k]   (TS form)
+// The next tile's S is issued as soon as the warps have read S, so it runs
+// while they form dS; dQ and the next dP run while they form the next P.
 constexpr int kDqStages = 3;
 
 template <int D, int RP>
-struct DqCfg {
-  static constexpr int KT = dq_key_rows(D, RP);
-  static constexpr int KH = KT / 2;  // key columns per warpgroup
-  static constexpr int align16(int x) { return (x + 15) & ~15; }
-  static constexpr int tDQ = 0, tS = D + RP, tDP = tS + KT, tDS = tDP + KT, tQ = align16(tDS + KT / 2),
-                       tDO = tQ + D / 2;
-  static_assert(tDO + D / 2 <= 512, "TMEM budget");
-  static_assert(KH == 48 || KH == 40, "warpgroup column split");
-};
-
-template <int D, int RP>
 struct DqSmem {
-  static constexpr int KT = DqCfg<D, RP>::KT;
-  static constexpr int kKChunk = KT * 128;             // one 64-column atom of a key tile
+  static constexpr int kKChunk = kQT * 128;            // one 64-column atom of a 112-row key tile
   static constexpr int kKAtoms = D / 64 + 1;           // K chunks + the padded R_k atom
   static constexpr int kRq = 128 * RP * 2;
   static constexpr int align(int x) { return (x + 1023) & ~1023; }
@@ -881,13 +867,12 @@ struct DqSmem {
   static constexpr int kVStage = (D / 64) * kKChunk;
   static constexpr int kQChunk = 128 * 128;             // one 64-column atom of a 128-row tile
   static constexpr int kQStage = (D / 64) * kQChunk;    // Q (then dO) staged in the V ring
-  static constexpr int kVRegion = kDqStages * kVStage > 2 * kQStage ? kDqStages * kVStage : 2 * kQStage;
-  static constexpr int oBar = align(oV + kVRegion);
+  static_assert(2 * kQStage <= kDqStages * kVStage, "Q and dO must fit in the V ring");
+  static constexpr int oBar = align(oV + kDqStages * kVStage);
   static constexpr int kNumBars = 24;
   static constexpr int oMisc = oBar + kNumBars * 8;
   static constexpr int kTotal = oMisc + 16 + 1024;
   static_assert(kKChunk % 1024 == 0, "swizzle atoms need 1024-byte alignment");
-  static_assert(kTotal <= kMaxDynamicSmem, "shared memory budget");
 };
 
 enum DqBar {
@@ -904,29 +889,9 @@ enum DqBar {
   kBAllDone = 18,
   kBQFull = 19,     // Q and dO tiles landed in the V ring
   kBStageFree = 20, // Q and dO copied to tensor memory; the V ring may be filled
-  kBDpRead = 21,    // warps have read dP (one arrival per warp)
-  kBDqDone = 22,    // dQ MMA of a tile complete (dS columns free)
 };
 
 constexpr int kDqThreads = 320;  // 8 softmax-gradient warps, producer, MMA
-
-// N consecutive TMEM columns of this warp's lanes (N = 40 or 48).
-template <int N>
-__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t* r) {
-  tmem_ld32(taddr, r);
-  if constexpr (N == 48) tmem_ld16(taddr + 32, r + 32);
-  if constexpr (N == 40) tmem_ld8(taddr + 32, r + 32);
-  tmem_ld_wait32(r);
-  if constexpr (N == 48) tmem_ld_wait16(r + 32);
-  if constexpr (N == 40) tmem_ld_wait8(r + 32);
-}
-// N packed columns (N = 20 or 24).
-template <int N>
-__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t* r) {
-  tmem_st16(taddr, r);
-  if constexpr (N == 24) tmem_st8(taddr + 16, r + 16);
-  if constexpr (N == 20) tmem_st4(taddr + 16, r + 16);
-}
 
 template <int D, int RP>
 __global__ void __launch_bounds__(kDqThreads, 1)
@@ -935,8 +900,6 @@ __global__ void __launch_bounds__(kDqThreads, 1)
                        const __grid_constant__ CUtensorMap tmRq, const __grid_constant__ CUtensorMap tmRk,
                        const BwdParams p) {
   using L = DqSmem<D, RP>;
-  using C = DqCfg<D, RP>;
-  constexpr int KT = C::KT, KH = C::KH;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::oBar);
@@ -944,25 +907,24 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::oMisc + 4);
 
   const ProblemDev& P = p.prob;
-  int m_blk, h;
+  const int h = blockIdx.y;
+  int m_blk;
   SeqInfo si;
-  if (P.varlen) {  // grid (table entry, head): one CTA per real query tile (table from the pre kernel)
-    h = blockIdx.y;
+  if (P.varlen) {  // one CTA per real query tile (table written by the pre kernel)
     const int4 e0 = p.tab_q[2 * blockIdx.x], e1 = p.tab_q[2 * blockIdx.x + 1];
     if (e0.x < 0) return;
     m_blk = e0.x;
     si.q_start = e0.y, si.k_start = e0.z, si.len_q = e0.w, si.len_k = e1.x, si.b = 0;
-  } else {  // grid (head, batch, query tile): the last, heaviest causal tile launches first
-    h = blockIdx.x;
-    m_blk = p.n_mblocks - 1 - static_cast<int>(blockIdx.z);
-    si = seq_info(P, blockIdx.y);
+  } else {
+    m_blk = p.n_mblocks - 1 - static_cast<int>(blockIdx.x);
+    si = seq_info(P, blockIdx.z);
   }
   const int q0 = m_blk * kBlockM;
   if (q0 >= si.len_q) return;
   const int hk = h / (P.heads / P.heads_kv);
   const bool graph = h < P.heads_graph;
   const int kv_end = P.causal ? min(si.len_k, q0 + kBlockM) : si.len_k;
-  const int n_tiles = kv_end > 0 ? (kv_end + KT - 1) / KT : 0;
+  const int n_tiles = kv_end > 0 ? (kv_end + kQT - 1) / kQT : 0;
   const int warp = warp_id();
   const int lane = lane_id();
   const int tid = threadIdx.x;
@@ -991,9 +953,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
     mbar_init(&bars[kBSFull], 1);
     mbar_init(&bars[kBDPFull], 1);
     mbar_init(&bars[kBSRead], 8);
-    mbar_init(&bars[kBDpRead], 8);
     mbar_init(&bars[kBDsReady], 8);
-    mbar_init(&bars[kBDqDone], 1);
     mbar_init(&bars[kBAllDone], 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -1006,8 +966,9 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tDQ = tmem + C::tDQ, tS = tmem + C::tS, tDP = tmem + C::tDP, tDS = tmem + C::tDS,
-                 tQ = tmem + C::tQ, tDO = tmem + C::tDO;
+  const uint32_t tDQ = tmem + 0, tS = tmem + 160, tDP = tmem + 272, tQ = tmem + 384, tDO = tmem + 448;
+  // TMEM column (relative to dP) of the packed bf16 dS for the 16 keys of k-step kk
+  auto packed_col = [](int kk) { return (kk < 4 ? 0 : 64) + (kk & 3) * 8; };
 
   if (warp == 8) {
     // ------------------------------------------------------------ producer
@@ -1027,7 +988,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       }
       auto load_k = [&](int j) {
         const int s = j % kDqStages;
-        const int krow = si.k_start + (n_tiles - 1 - j) * KT;
+        const int krow = si.k_start + (n_tiles - 1 - j) * kQT;
         uint8_t* sk = smem + L::oK + s * L::kKStage;
         mbar_expect_tx(&bars[kBKFull + s], (D / 64) * L::kKChunk + (graph ? L::kKChunk : 0));
 #pragma unroll
@@ -1037,7 +998,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       };
       auto load_v = [&](int j) {
         const int s = j % kDqStages;
-        const int krow = si.k_start + (n_tiles - 1 - j) * KT;
+        const int krow = si.k_start + (n_tiles - 1 - j) * kQT;
         uint8_t* sv = smem + L::oV + s * L::kVStage;
         mbar_expect_tx(&bars[kBVFull + s], (D / 64) * L::kKChunk);
 #pragma unroll
@@ -1051,18 +1012,17 @@ __global__ void __launch_bounds__(kDqThreads, 1)
         for (int j = 0; j < n_first; ++j) load_v(j);
         for (int j = kDqStages; j < n_tiles; ++j) {
           const uint32_t par = ((j / kDqStages) - 1) & 1;
-          // V(j - 3) is released by dP(j - 3), which runs before dQ(j - 3) releases K(j - 3)
-          if (!mbar_wait(&bars[kBVEmpty + j % kDqStages], par, abort_flag, 802)) break;
-          load_v(j);
           if (!mbar_wait(&bars[kBKEmpty + j % kDqStages], par, abort_flag, 801)) break;
           load_k(j);
+          if (!mbar_wait(&bars[kBVEmpty + j % kDqStages], par, abort_flag, 802)) break;
+          load_v(j);
         }
       }
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_s = make_idesc_bf16(128, KT, 0, 0);        // S, dP (N = KT keys)
+      constexpr uint32_t idesc_s = make_idesc_bf16(128, kQT, 0, 0);       // S, dP (N = 112 keys)
       constexpr uint32_t idesc_dq = make_idesc_bf16(128, D, 0, 1);        // dQ only (vanilla heads)
       constexpr uint32_t idesc_dqr = make_idesc_bf16(128, D + RP, 0, 1);  // [dQ | dS R_k]
       const uint32_t r_layout = r_layout_of(RP);
@@ -1119,39 +1079,36 @@ __global__ void __launch_bounds__(kDqThreads, 1)
         }
       }
       for (int j = 0; ok && j < n_tiles; ++j) {
-        const bool more = j + 1 < n_tiles;
-        const int s1 = (j + 1) % kDqStages;
-        const uint32_t par1 = ((j + 1) / kDqStages) & 1;
-        // next S as soon as the warps have read S (it overlaps their P and dS work)
+        // next tile's S as soon as the warps have read S (it overlaps their dS work)
         if (!mbar_wait_spin(&bars[kBSRead], j & 1, abort_flag, 904)) break;
-        if (more) {
-          if (!mbar_wait_spin(&bars[kBKFull + s1], par1, abort_flag, 905)) break;
+        if (j + 1 < n_tiles) {
+          const int s1 = (j + 1) % kDqStages;
+          if (!mbar_wait_spin(&bars[kBKFull + s1], ((j + 1) / kDqStages) & 1, abort_flag, 905)) break;
           tc_fence_after();
           issue_s(j + 1);
         }
-        // next dP as soon as the warps have read dP (it overlaps their dS work)
-        if (!mbar_wait_spin(&bars[kBDpRead], j & 1, abort_flag, 909)) break;
-        if (more) {
-          if (!mbar_wait_spin(&bars[kBVFull + s1], par1, abort_flag, 908)) break;
-          tc_fence_after();
-          issue_dp(j + 1);
-        }
-        // [dQ | dS R_k] += dS [K | R_k]
+        // [dQ | dS R_k] += dS [K | R_k], then the next dP.  Both waits come
+        // before the two MMA groups: a wait issued behind queued MMAs only
+        // returns once the tensor pipe has nearly drained them.
         if (!mbar_wait_spin(&bars[kBDsReady], j & 1, abort_flag, 906)) break;
+        if (j + 1 < n_tiles &&
+            !mbar_wait_spin(&bars[kBVFull + (j + 1) % kDqStages], ((j + 1) / kDqStages) & 1, abort_flag, 908))
+          break;
         tc_fence_after();
         const uint32_t sK = stage_k(j);
 #pragma unroll
-        for (int kk = 0; kk < KT / 16; ++kk)
-          mma_ts(tDQ, tDS + kk * 8, make_sdesc(sK + kk * 2048, L::kKChunk, 1024, kSwizzle128B),
+        for (int kk = 0; kk < kQT / 16; ++kk)
+          mma_ts(tDQ, tDP + packed_col(kk), make_sdesc(sK + kk * 2048, L::kKChunk, 1024, kSwizzle128B),
                  graph ? idesc_dqr : idesc_dq, (j > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(&bars[kBDqDone]);
         mma_commit(&bars[kBKEmpty + (j % kDqStages)]);
+        // next tile's dP (overwrites dS, read in order above)
+        if (j + 1 < n_tiles) issue_dp(j + 1);
       }
       if (ok) mma_commit(&bars[kBAllDone]);
     }
   } else {
     // ------------------------------------------------------------ softmax-gradient warps 0-7 (query rows)
-    const int wg = warp >> 2;  // key columns [KH*wg, KH*wg + KH)
+    const int wg = warp >> 2;  // key columns [64*wg, min(64*wg+64, 112))
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int t = tid & 127;
     const int q_local = q0 + t;
@@ -1182,55 +1139,71 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[kBRqReady]);
     }
-    const uint32_t tSw = tS + lane_base + KH * wg, tDPw = tDP + lane_base + KH * wg;
-    const uint32_t tDSw = tDS + lane_base + (KH / 2) * wg;
+    const uint32_t tSw = tS + lane_base + 64 * wg, tDPw = tDP + lane_base + 64 * wg;
     for (int j = 0; ok && j < n_tiles; ++j) {
       if (!mbar_wait(&bars[kBSFull], j & 1, abort_flag, 1002)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      // phase 1: read S (releasing it for the next tile), P = exp2(S*c - LSE2) for this warp's keys
-      float pf[KH];
-      {
-        uint32_t sv[KH];
-        tmem_ld_cols<KH>(tSw, sv);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[kBSRead]);
-        const int col0 = (n_tiles - 1 - j) * KT + KH * wg;
-        if (col0 + KH > limit) {
+      // phase 1 (overlaps the dP MMA): P = exp2(S*c - LSE2) for this warp's keys
+      float pf[64];
 #pragma unroll
-          for (int k = 0; k < KH; ++k)  // masked key columns: -inf exponent, ex2(-inf) = 0
-            if (col0 + k >= limit) sv[k] = __float_as_uint(-INFINITY);
+      for (int c = 0; c < 2; ++c) {
+        uint32_t sv[32];
+        const int col0 = (n_tiles - 1 - j) * kQT + 64 * wg + 32 * c;
+        if (c == 0 || wg == 0) {
+          tmem_ld32(tSw + 32 * c, sv);
+          tmem_ld_wait32(sv);
+          if (col0 + 32 > limit) {
+#pragma unroll
+            for (int k = 0; k < 32; ++k)  // masked key columns: -inf exponent, ex2(-inf) = 0
+              if (col0 + k >= limit) sv[k] = __float_as_uint(-INFINITY);
+          }
+#pragma unroll
+          for (int k = 0; k < 32; ++k) pf[32 * c + k] = ex2(fmaf(__uint_as_float(sv[k]), sl2, -lse2));
+        } else {  // warpgroup 1, keys 96..111 of the tile
+          tmem_ld16(tSw + 32, sv);
+          tmem_ld_wait16(sv);
+          if (col0 + 16 > limit) {
+#pragma unroll
+            for (int k = 0; k < 16; ++k)
+              if (col0 + k >= limit) sv[k] = __float_as_uint(-INFINITY);
+          }
+#pragma unroll
+          for (int k = 0; k < 16; ++k) pf[32 + k] = ex2(fmaf(__uint_as_float(sv[k]), sl2, -lse2));
+#pragma unroll
+          for (int k = 16; k < 32; ++k) pf[32 + k] = 0.f;
         }
-#pragma unroll
-        for (int k = 0; k < KH; ++k) pf[k] = ex2(fmaf(__uint_as_float(sv[k]), sl2, -lse2));
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[kBSRead]);
       if (!mbar_wait(&bars[kBDPFull], j & 1, abort_flag, 1004)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      // phase 2: read dP (releasing it for the next tile), dS = P (dP - Delta) into the dS columns
-      uint32_t dd[KH / 2];
-      {
-        uint32_t dp[KH];
-        tmem_ld_cols<KH>(tDPw, dp);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[kBDpRead]);
+      // phase 2 (overlaps the next S MMA): dS = P (dP - Delta) into this warp's dP columns
+      uint32_t dd[32];
 #pragma unroll
-        for (int k = 0; k < KH; k += 2)
-          dd[k >> 1] = pack_bf16(pf[k] * (__uint_as_float(dp[k]) - delta), pf[k + 1] * (__uint_as_float(dp[k + 1]) - delta));
+      for (int c = 0; c < 2; ++c) {
+        uint32_t dp[32];
+        if (c == 0 || wg == 0) {
+          tmem_ld32(tDPw + 32 * c, dp);
+          tmem_ld_wait32(dp);
+        } else {
+          tmem_ld16(tDPw + 32, dp);
+          tmem_ld_wait16(dp);
+#pragma unroll
+          for (int k = 16; k < 32; ++k) dp[k] = 0u;  // beyond the 112-column tile
+        }
+#pragma unroll
+        for (int k = 0; k < 32; k += 2)
+          dd[16 * c + (k >> 1)] = pack_bf16(pf[32 * c + k] * (__uint_as_float(dp[k]) - delta),
+                                            pf[32 * c + k + 1] * (__uint_as_float(dp[k + 1]) - delta));
       }
-      // the dS columns are free once the previous tile's dQ MMA has read them
-      if (j > 0 && !mbar_wait(&bars[kBDqDone], (j - 1) & 1, abort_flag, 1005)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      tmem_st_cols<KH / 2>(tDSw, dd);
+      tmem_st32(tDPw, dd);  // columns this warp has already read
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
@@ -1324,7 +1297,7 @@ cudaError_t launch_bwd_t(const BwdMaps& m, const BwdParams& p, cudaStream_t stre
     auto kern = fna2_bwd_dkdv_kernel<D, RP>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
     if (e != cudaSuccess) return e;
-    const dim3 grid = p.prob.varlen ? dim3(p.tab_k_len, p.prob.heads_kv, 1) : dim3(p.prob.heads_kv, p.batch, p.n_nblocks);
+    dim3 grid(p.prob.varlen ? p.tab_k_len : p.n_nblocks, p.prob.heads_kv, p.prob.varlen ? 1 : p.batch);
     kern<<<grid, kDkdvThreads, L::kTotal, stream>>>(m.qS, m.k, m.v, m.dOS, m.rqS, m.rk, p);
     e = cudaGetLastError();
     if (e == cudaSuccess && ev) e = cudaEventRecord(ev[2], stream);
@@ -1335,7 +1308,7 @@ cudaError_t launch_bwd_t(const BwdMaps& m, const BwdParams& p, cudaStream_t stre
     auto kern = fna2_bwd_dq_kernel<D, RP>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
     if (e != cudaSuccess) return e;
-    const dim3 grid = p.prob.varlen ? dim3(p.tab_q_len, p.prob.heads, 1) : dim3(p.prob.heads, p.batch, p.n_mblocks);
+    dim3 grid(p.prob.varlen ? p.tab_q_len : p.n_mblocks, p.prob.heads, p.prob.varlen ? 1 : p.batch);
     kern<<<grid, kDqThreads, L::kTotal, stream>>>(m.q, m.kDq, m.vDq, m.dO, m.rq, m.rkDq, p);
     e = cudaGetLastError();
     if (e == cudaSuccess && ev) e = cudaEventRecord(ev[3], stream);

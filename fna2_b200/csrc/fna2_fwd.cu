@@ -109,15 +109,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::oMisc + 4);
 
   const ProblemDev& P = p.prob;
-  // grid (head, batch/sequence, pair): the pair index varies slowest and counts
-  // down, so the heaviest causal pairs of every head and sequence launch first
-  // (longest-processing-time order for the tail of the grid)
+  // grid (pair, head, batch/sequence): the CTAs of one head and sequence run
+  // together and share its K/V tiles in L2; within them the heaviest causal
+  // pairs start first
   const int n_pairs = (p.n_mblocks + 1) / 2;
-  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.z);
-  const int h = blockIdx.x;
-  const SeqInfo si = seq_info(P, blockIdx.y);
+  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.x);
+  const int h = blockIdx.y;
+  const SeqInfo si = seq_info(P, blockIdx.z);
   if (!seq_ok(P, si)) {  // inconsistent cu_seqlens: skip the sequence, report it once
-    if (blockIdx.x == 0 && blockIdx.z == 0 && threadIdx.x == 0) atomicCAS(&g_device_error, 0, kStatusBadSeqFwd);
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) atomicCAS(&g_device_error, 0, kStatusBadSeqFwd);
     return;
   }
   const int q0 = pair * 2 * kBlockM;
@@ -449,7 +449,7 @@ cudaError_t launch_fwd_t(const CUtensorMap& q, const CUtensorMap& k, const CUten
   auto kern = fna2_fwd_kernel<D, RP>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
   if (e != cudaSuccess) return e;
-  dim3 grid(grid_y, grid_z, (p.n_mblocks + 1) / 2);
+  dim3 grid((p.n_mblocks + 1) / 2, grid_y, grid_z);
   kern<<<grid, kFwdThreads, L::kTotal, stream>>>(q, k, v, rq, rk, p);
   return cudaGetLastError();
 }

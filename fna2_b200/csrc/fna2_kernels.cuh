@@ -19,10 +19,10 @@ constexpr float kEps = 1e-6f;  // O = acc/(l+1e-6), LSE = m + log(l+1e-6)  (flas
 // P^T fit in the 512 TMEM columns.
 __host__ __device__ constexpr int dkdv_query_rows(int D, int RP) { return (D == 128 && RP == 32) ? 64 : 96; }
 
-// Key rows per tile of the query-stationary (dQ) backward kernel: the largest
-// multiple of 16 (of 96 at most) for which [dQ | dR_q], S, dP, a separate
-// packed dS, Q and dO fit in the 512 TMEM columns.
-__host__ __device__ constexpr int dq_key_rows(int D, int RP) { return (D == 128 && RP == 32) ? 80 : 96; }
+// Key rows per tile of the query-stationary (dQ) backward kernel: [dQ | dR_q]
+// (160 columns), S and dP (112 each; dS is written over dP's first columns),
+// Q and dO (64 each) fill the 512 TMEM columns.
+__host__ __device__ constexpr int dq_key_rows(int /*D*/, int /*RP*/) { return 112; }
 
 // Sequence bounds of one (batch or packed sequence) index. Dense problems have
 // all sequences of length seqlen_q/seqlen_k starting at row 0 of their batch.

@@ -64,8 +64,8 @@ typedef struct Fna2Tensor {
 
 typedef struct Fna2Problem {
   int32_t batch;       /* dense: B.  varlen: number of packed sequences N */
-  int32_t seqlen_q;    /* dense: S.  varlen: max_seqlen_q (>= every q length); <= 65535*128 */
-  int32_t seqlen_k;    /* dense: S.  varlen: max_seqlen_k (>= every k length); <= 65535*128 */
+  int32_t seqlen_q;    /* dense: S.  varlen: max_seqlen_q (>= every q length) */
+  int32_t seqlen_k;    /* dense: S.  varlen: max_seqlen_k (>= every k length) */
   int32_t total_q;     /* varlen: rows of the packed q tensor (T_q); dense: unused */
   int32_t total_k;     /* varlen: rows of the packed k/v tensors (T_k); dense: unused */
   int32_t heads;       /* H */
