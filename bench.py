@@ -605,7 +605,7 @@ def run_e2e(args, dist, world, rank, local, dev, stream, q, k, v, rq, rk, do, gs
            "h2d_bytes_per_step": h2d_all, "d2h_bytes_per_step": d2h_all, "ms_per_step": ems}
 
     # copy ceiling of the host link: the same bytes, the same group copies, no compute
-    dev_out = [torch.empty_like(t) for t in host_out]
+    dev_out = [torch.empty(t.shape, dtype=t.dtype, device=dev) for t in host_out]
 
     def copies(inp, outp):
         def fn():
