@@ -469,7 +469,7 @@ def run_gpu(args, w):
             "e2e": e2e,
             "copy_ceiling": ceiling,
             "sharding_check": check,
-            "gpu_launches": 4 * K,
+            "gpu_launches": 5 * K,  # per step: forward tile table, forward, backward pre-pass, dK/dV, dQ
             "clocks": clk,
             "cpu_baseline": cpu,
             "device_status": status,

@@ -12,7 +12,7 @@ from typing import Optional
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("FNA2_LIB", os.path.join(HERE, "libfna2_b200.so"))
 
-FNA2_ABI_VERSION = 3
+FNA2_ABI_VERSION = 4
 FNA2_OK = 0
 FNA2_ERR_INVALID = -1
 FNA2_ERR_CUDA = -2
@@ -20,7 +20,7 @@ FNA2_ERR_WORKSPACE = -3
 
 EXPORTED = ["fna2_fwd", "fna2_bwd", "fna2_bwd_workspace_size", "fna2_last_error", "fna2_device_status",
             "fna2_abi_version", "fna2_bwd_noalloc", "fna2_qk_prep_fwd", "fna2_qk_prep_bwd", "fna2_decode", "fna2_decode_workspace_size",
-            "fna2_debug_watchdog"]
+            "fna2_debug_watchdog", "fna2_fwd_workspace_size"]
 FNA2_DTYPE_F32 = 0
 FNA2_DTYPE_BF16 = 1
 NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024  # FNA2_NOALLOC_SCRATCH_BYTES
@@ -61,6 +61,8 @@ class Fna2FwdArgs(ctypes.Structure):
         ("out", Fna2Tensor),
         ("lse", ctypes.c_void_p),
         ("launch_events", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
     ]
 
 
@@ -176,6 +178,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.fna2_decode.restype = ctypes.c_int
     lib.fna2_decode_workspace_size.argtypes = [ctypes.POINTER(Fna2DecodeArgs)]
     lib.fna2_decode_workspace_size.restype = ctypes.c_size_t
+    lib.fna2_fwd_workspace_size.argtypes = [ctypes.POINTER(Fna2Problem)]
+    lib.fna2_fwd_workspace_size.restype = ctypes.c_size_t
     lib.fna2_bwd_workspace_size.argtypes = [ctypes.POINTER(Fna2Problem)]
     lib.fna2_bwd_workspace_size.restype = ctypes.c_size_t
     lib.fna2_last_error.argtypes = []

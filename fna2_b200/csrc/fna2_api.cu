@@ -237,6 +237,12 @@ extern "C" int fna2_fwd(const Fna2FwdArgs* a, void* stream) {
     if (int rc = check_tensor(a->r_k, "r_k", s.varlen)) return rc;
     FNA2_CHECK(a->graph_scale != nullptr, "graph_scale: null pointer");
   }
+  if (s.varlen) {  // the table of real query-tile pairs
+    const size_t need = fwd_workspace_bytes(true, s.rows_q(), s.B);
+    if (a->workspace_bytes < need || a->workspace == nullptr)
+      return fail(FNA2_ERR_WORKSPACE, "forward workspace too small: %zu < %zu bytes", a->workspace_bytes, need);
+    FNA2_CHECK((reinterpret_cast<uintptr_t>(a->workspace) & 255u) == 0, "workspace must be 256-byte aligned");
+  }
   CUtensorMap tq, tk, tv, trq, trk;
   if (int rc = map_qkv(&tq, a->q, s, s.rows_q(), s.H, "q")) return rc;
   if (int rc = map_qkv(&tk, a->k, s, s.rows_k(), s.HKV, "k")) return rc;
@@ -258,12 +264,21 @@ extern "C" int fna2_fwd(const Fna2FwdArgs* a, void* stream) {
   p.lse = a->lse;
   p.lse_sbh = s.rows_q();
   p.n_mblocks = (s.Sq + kBlockM - 1) / kBlockM;
+  p.tab = s.varlen ? static_cast<int4*>(a->workspace) : nullptr;
+  p.tab_len = s.varlen ? fwd_tab_len(s.rows_q(), s.B) : 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaEvent_t* ev = reinterpret_cast<cudaEvent_t*>(a->launch_events);
   if (ev) FNA2_CUDA(cudaEventRecord(ev[0], st));
   FNA2_CUDA(launch_fwd(s.D, s.RP, tq, tk, tv, trq, trk, p, s.H, s.B, st));
   if (ev) FNA2_CUDA(cudaEventRecord(ev[1], st));
   return FNA2_OK;
+}
+
+extern "C" size_t fna2_fwd_workspace_size(const Fna2Problem* prob) {
+  if (!prob) return 0;
+  Shape s;
+  if (check_problem(*prob, &s)) return 0;
+  return fwd_workspace_bytes(s.varlen, s.rows_q(), s.B);
 }
 
 extern "C" size_t fna2_bwd_workspace_size(const Fna2Problem* prob) {

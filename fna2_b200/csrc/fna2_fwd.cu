@@ -109,17 +109,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::oMisc + 4);
 
   const ProblemDev& P = p.prob;
-  // grid (pair, head, batch/sequence): the CTAs of one head and sequence run
-  // together and share its K/V tiles in L2; within them the heaviest causal
-  // pairs start first
-  const int n_pairs = (p.n_mblocks + 1) / 2;
-  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.x);
-  const int h = blockIdx.y;
-  const SeqInfo si = seq_info(P, blockIdx.z);
-  if (!seq_ok(P, si)) {  // inconsistent cu_seqlens: skip the sequence, report it once
-    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) atomicCAS(&g_device_error, 0, kStatusBadSeqFwd);
-    return;
+  int pair;
+  SeqInfo si;
+  if (P.varlen) {
+    // grid (table entry, head): one CTA per real pair of query tiles; the table
+    // lists each sequence's pairs heaviest first, so the CTAs of one head and
+    // sequence run together and share its K/V tiles in L2
+    const int4 e0 = p.tab[2 * blockIdx.x], e1 = p.tab[2 * blockIdx.x + 1];
+    if (e0.x < 0) return;
+    pair = e0.x;
+    si.q_start = e0.y, si.k_start = e0.z, si.len_q = e0.w, si.len_k = e1.x, si.b = 0;
+  } else {  // grid (pair, head, batch), heaviest causal pairs first
+    pair = (p.n_mblocks + 1) / 2 - 1 - static_cast<int>(blockIdx.x);
+    si = seq_info(P, blockIdx.z);
   }
+  const int h = blockIdx.y;
   const int q0 = pair * 2 * kBlockM;
   if (q0 >= si.len_q) return;
   const int hk = h / (P.heads / P.heads_kv);
@@ -440,6 +444,58 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// varlen: table of the real pairs of query tiles (one CTA, before the forward)
+// ---------------------------------------------------------------------------
+// Entries per sequence, in packing order, heaviest causal pair first.  A
+// sequence whose cu_seqlens entries are inconsistent (seq_ok) gets no entries
+// and the call records kStatusBadSeqFwd.  A block-wide scan runs over chunks of
+// 128 sequences, carrying the running offset from chunk to chunk.
+inline int fwd_tab_len(int rows_q, int n_seqs) { return (rows_q + 2 * kBlockM - 1) / (2 * kBlockM) + n_seqs; }
+
+inline size_t fwd_workspace_bytes(bool varlen, int rows_q, int n_seqs) {
+  return varlen ? static_cast<size_t>(fwd_tab_len(rows_q, n_seqs)) * 32 : 0;
+}
+
+__global__ void __launch_bounds__(128) fna2_fwd_table_kernel(const FwdParams p, int n_seqs) {
+  const ProblemDev& P = p.prob;
+  __shared__ int scan_s[4];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int carry = 0;
+  for (int base = 0; base < n_seqs; base += 128) {
+    const int z = base + static_cast<int>(threadIdx.x);
+    SeqInfo e;
+    e.q_start = e.k_start = e.len_q = e.len_k = 0;
+    e.b = 0;
+    if (z < n_seqs) {
+      e.q_start = __ldg(P.cu_q + z), e.len_q = __ldg(P.cu_q + z + 1) - e.q_start;
+      e.k_start = __ldg(P.cu_k + z), e.len_k = __ldg(P.cu_k + z + 1) - e.k_start;
+      if (!seq_ok(P, e)) {  // skipped before any access; reported once per call
+        atomicCAS(&g_device_error, 0, kStatusBadSeqFwd);
+        e.len_q = 0;
+      }
+    }
+    const int np = (e.len_q + 2 * kBlockM - 1) / (2 * kBlockM);  // >= 0
+    int incl = np;  // inclusive scan within the warp
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += u;
+    }
+    if (lane == 31) scan_s[w] = incl;
+    __syncthreads();
+    int off = carry + incl - np;
+    for (int i = 0; i < w; ++i) off += scan_s[i];
+    for (int t = 0; t < np && off + t < p.tab_len; ++t) {
+      p.tab[2 * (off + t)] = make_int4(np - 1 - t, e.q_start, e.k_start, e.len_q);
+      p.tab[2 * (off + t) + 1] = make_int4(e.len_k, z, 0, 0);
+    }
+    carry += scan_s[0] + scan_s[1] + scan_s[2] + scan_s[3];
+    __syncthreads();
+  }
+  for (int i = carry + static_cast<int>(threadIdx.x); i < p.tab_len; i += 128) p.tab[2 * i] = make_int4(-1, 0, 0, 0);
+}
+
+// ---------------------------------------------------------------------------
 // host-side launch helper (called from fna2_api.cu)
 // ---------------------------------------------------------------------------
 template <int D, int RP>
@@ -449,7 +505,12 @@ cudaError_t launch_fwd_t(const CUtensorMap& q, const CUtensorMap& k, const CUten
   auto kern = fna2_fwd_kernel<D, RP>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
   if (e != cudaSuccess) return e;
-  dim3 grid((p.n_mblocks + 1) / 2, grid_y, grid_z);
+  if (p.prob.varlen) {
+    fna2_fwd_table_kernel<<<1, 128, 0, stream>>>(p, grid_z);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  const dim3 grid = p.prob.varlen ? dim3(p.tab_len, grid_y, 1) : dim3((p.n_mblocks + 1) / 2, grid_y, grid_z);
   kern<<<grid, kFwdThreads, L::kTotal, stream>>>(q, k, v, rq, rk, p);
   return cudaGetLastError();
 }

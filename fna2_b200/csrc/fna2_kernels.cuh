@@ -84,7 +84,12 @@ struct FwdParams {
   int64_t o_sb, o_sh, o_sr;  // element strides (batch, head, row); column stride is 1
   float* lse;                // index (b*H + h) * lse_sbh + row
   int64_t lse_sbh;
-  int n_mblocks;             // grid.x
+  int n_mblocks;             // dense: query tiles per sequence (grid.x = pairs of them)
+  // varlen: table of the real pairs of 128-row query tiles, 8 ints per entry
+  // {pair, q_start, k_start, len_q, len_k, 0, 0, 0} (pair < 0: past the end),
+  // written by fna2_fwd_table_kernel; the forward launches tab_len CTAs per head
+  int4* tab;
+  int tab_len;
 };
 
 struct BwdParams {

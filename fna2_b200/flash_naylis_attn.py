@@ -169,6 +169,11 @@ def _fna2_forward(q, k, v, r_q, r_k, gs, softmax_scale, is_causal, cu_q=None, cu
     a.out = _desc(out, varlen)
     a.lse = lse.data_ptr()
     a.launch_events, keep = _events_arg(launch_events)
+    ws = None
+    if varlen:  # the table of real query-tile pairs (caching allocator)
+        ws_bytes = lib.fna2_fwd_workspace_size(ctypes.byref(a.prob))
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q.device)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     _lib.check(lib.fna2_fwd(ctypes.byref(a), _stream()), "fna2_fwd")
     return out, lse
 

@@ -50,7 +50,7 @@
 extern "C" {
 #endif
 
-#define FNA2_ABI_VERSION 3
+#define FNA2_ABI_VERSION 4
 
 #define FNA2_OK 0
 #define FNA2_ERR_INVALID (-1)
@@ -87,7 +87,12 @@ typedef struct Fna2FwdArgs {
   Fna2Tensor out;       /* same shape as q */
   float* lse;           /* [B,H,S] or [H,T_q] */
   void** launch_events; /* optional (NULL = off): 2 cudaEvent_t recorded on `stream`
-                           before and after the forward kernel, for per-kernel timing */
+                           before and after the forward (for packed batches: the tile
+                           table kernel and the forward kernel), for per-kernel timing */
+  void* workspace;      /* packed batches: device scratch, >= fna2_fwd_workspace_size()
+                           bytes, 256-B aligned (the table of real query-tile pairs:
+                           32 B per entry, ceil(T_q/256) + N entries); dense: unused */
+  size_t workspace_bytes;
 } Fna2FwdArgs;
 
 typedef struct Fna2BwdArgs {
@@ -103,6 +108,12 @@ typedef struct Fna2BwdArgs {
   void** launch_events;      /* optional (NULL = off): 4 cudaEvent_t recorded on `stream` before the
                                 pre-pass, after it, after the dK/dV kernel and after the dQ kernel */
 } Fna2BwdArgs;
+
+/* Bytes of device scratch fna2_fwd needs for this problem (0 for dense
+ * problems or if invalid).  The reference's forward launcher allocates none: its
+ * varlen grid is (tiles of max_seqlen) x heads x sequences (flash_naylis_attn.py:
+ * 786-793); this one launches one CTA per real pair of query tiles from the table. */
+size_t fna2_fwd_workspace_size(const Fna2Problem* prob);
 
 /* Forward: writes out and lse.  Replaces _fna2_forward / _fna2_forward_varlen. */
 int fna2_fwd(const Fna2FwdArgs* args, void* stream);

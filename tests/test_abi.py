@@ -152,6 +152,26 @@ def test_empty_problem_is_a_no_op():
     assert lib.fna2_fwd(ctypes.byref(a), None) == _lib.FNA2_OK
 
 
+def test_forward_workspace_size_and_check():
+    """Packed forwards need the tile table (32 B per entry, ceil(T/256) + N
+    entries); dense ones need none.  A packed call without it fails on the host."""
+    lib = _lib.load()
+    dense = _fwd_args()
+    assert lib.fna2_fwd_workspace_size(ctypes.byref(dense.prob)) == 0
+    a = _fwd_args(batch=3, seqlen_q=300, seqlen_k=300, total_q=700, total_k=700)
+    a.prob.cu_seqlens_q = a.prob.cu_seqlens_k = 0x2000  # device pointers are not read on the host
+    n = lib.fna2_fwd_workspace_size(ctypes.byref(a.prob))
+    assert n == ((700 + 255) // 256 + 3) * 32
+    for name in ("q", "k", "v", "out", "r_q", "r_k"):
+        d = getattr(a, name)
+        d.ptr = 0x10000
+        d.stride[:] = (0, 128, 2 * 128, 1) if name not in ("r_q", "r_k") else (0, 16, 2 * 16, 1)
+    a.graph_scale = 0x10000
+    a.lse = 0x10000
+    rc = lib.fna2_fwd(ctypes.byref(a), None)
+    assert rc == _lib.FNA2_ERR_WORKSPACE and "forward workspace" in lib.fna2_last_error().decode()
+
+
 def test_workspace_size():
     lib = _lib.load()
     a = _fwd_args()

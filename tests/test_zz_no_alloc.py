@@ -72,6 +72,8 @@ def test_noalloc_backward_matches_workspace_backward_twice():
     fa.graph_scale = t["gs"].data_ptr()
     fa.out = _desc(t["out"], True)
     fa.lse = t["lse"].data_ptr()
+    fws = torch.empty(lib.fna2_fwd_workspace_size(ctypes.byref(prob)), dtype=torch.uint8, device=dev)
+    fa.workspace, fa.workspace_bytes = fws.data_ptr(), fws.numel()
     _lib.check(lib.fna2_fwd(ctypes.byref(fa), stream), "fna2_fwd")
 
     # existing entry point with a caller-provided workspace
