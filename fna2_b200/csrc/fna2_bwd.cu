@@ -891,7 +891,8 @@ enum DqBar {
   kBStageFree = 20, // Q and dO copied to tensor memory; the V ring may be filled
 };
 
-constexpr int kDqThreads = 320;  // 8 softmax-gradient warps, producer, MMA
+constexpr int kDqThreads = 352;  // 8 softmax-gradient warps, producer, MMA issuer, its waiter
+constexpr uint32_t kDqHandoffBar = 1;  // named barrier of the issuer / waiter rendezvous
 
 template <int D, int RP>
 __global__ void __launch_bounds__(kDqThreads, 1)
@@ -1021,43 +1022,47 @@ __global__ void __launch_bounds__(kDqThreads, 1)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc_s = make_idesc_bf16(128, kQT, 0, 0);       // S, dP (N = 112 keys)
-      constexpr uint32_t idesc_dq = make_idesc_bf16(128, D, 0, 1);        // dQ only (vanilla heads)
-      constexpr uint32_t idesc_dqr = make_idesc_bf16(128, D + RP, 0, 1);  // [dQ | dS R_k]
-      const uint32_t r_layout = r_layout_of(RP);
-      const uint32_t r_sbo = 8 * RP * 2;
-      const uint32_t sRq = smem_u32(smem + L::oRq);
-      auto stage_k = [&](int j) { return smem_u32(smem + L::oK + (j % kDqStages) * L::kKStage); };
-      auto stage_v = [&](int j) { return smem_u32(smem + L::oV + (j % kDqStages) * L::kVStage); };
-      auto issue_s = [&](int j) {  // S = Q K^T (+ R~_q R_k^T)
-        const uint32_t sK = stage_k(j);
+    // The whole warp follows the hand-off sequence below; lane 0 issues.  It
+    // learns that operands are ready only through pair_rendezvous with the
+    // waiter warp (warp 10), so it never touches memory behind its queued MMAs.
+    const bool leader = lane == 0;
+    constexpr uint32_t idesc_s = make_idesc_bf16(128, kQT, 0, 0);       // S, dP (N = 112 keys)
+    constexpr uint32_t idesc_dq = make_idesc_bf16(128, D, 0, 1);        // dQ only (vanilla heads)
+    constexpr uint32_t idesc_dqr = make_idesc_bf16(128, D + RP, 0, 1);  // [dQ | dS R_k]
+    const uint32_t r_layout = r_layout_of(RP);
+    const uint32_t r_sbo = 8 * RP * 2;
+    const uint32_t sRq = smem_u32(smem + L::oRq);
+    auto stage_k = [&](int j) { return smem_u32(smem + L::oK + (j % kDqStages) * L::kKStage); };
+    auto stage_v = [&](int j) { return smem_u32(smem + L::oV + (j % kDqStages) * L::kVStage); };
+    auto issue_s = [&](int j) {  // S = Q K^T (+ R~_q R_k^T)
+      const uint32_t sK = stage_k(j);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          mma_ts(tS, tQ + kk * 8, make_sdesc(sK + (kk >> 2) * L::kKChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B),
-                 idesc_s, kk > 0);
-        if (graph) {
-          const uint32_t sRk = sK + (D / 64) * L::kKChunk;
+      for (int kk = 0; kk < D / 16; ++kk)
+        mma_ts(tS, tQ + kk * 8, make_sdesc(sK + (kk >> 2) * L::kKChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B),
+               idesc_s, kk > 0);
+      if (graph) {
+        const uint32_t sRk = sK + (D / 64) * L::kKChunk;
 #pragma unroll
-          for (int kk = 0; kk < RP / 16; ++kk)
-            mma_ss(tS, make_sdesc(sRq + kk * 32, 16, r_sbo, r_layout), make_sdesc(sRk + kk * 32, 16, 1024, kSwizzle128B),
-                   idesc_s, 1);
-        }
-        mma_commit(&bars[kBSFull]);
-      };
-      auto issue_dp = [&](int j) {  // dP = dO V^T
-        const uint32_t sV = stage_v(j);
+        for (int kk = 0; kk < RP / 16; ++kk)
+          mma_ss(tS, make_sdesc(sRq + kk * 32, 16, r_sbo, r_layout), make_sdesc(sRk + kk * 32, 16, 1024, kSwizzle128B),
+                 idesc_s, 1);
+      }
+      mma_commit(&bars[kBSFull]);
+    };
+    auto issue_dp = [&](int j) {  // dP = dO V^T
+      const uint32_t sV = stage_v(j);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          mma_ts(tDP, tDO + kk * 8, make_sdesc(sV + (kk >> 2) * L::kKChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B),
-                 idesc_s, kk > 0);
-        mma_commit(&bars[kBDPFull]);
-        mma_commit(&bars[kBVEmpty + (j % kDqStages)]);
-      };
-      // Q and dO: shared memory (V ring) -> tensor memory, in the TS A-operand layout
-      bool ok = mbar_wait(&bars[kBQFull], 0, abort_flag, 901);
-      if (ok) {
-        tc_fence_after();
+      for (int kk = 0; kk < D / 16; ++kk)
+        mma_ts(tDP, tDO + kk * 8, make_sdesc(sV + (kk >> 2) * L::kKChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B),
+               idesc_s, kk > 0);
+      mma_commit(&bars[kBDPFull]);
+      mma_commit(&bars[kBVEmpty + (j % kDqStages)]);
+    };
+    // hand-off 1: Q and dO landed -> shared memory (V ring) to tensor memory, TS A-operand layout
+    bool ok = pair_rendezvous(kDqHandoffBar, true);
+    if (ok) {
+      tc_fence_after();
+      if (leader) {
         const uint32_t sQ = smem_u32(smem + L::oV), sDo = sQ + L::kQStage;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -1067,34 +1072,36 @@ __global__ void __launch_bounds__(kDqThreads, 1)
         }
         mma_commit(&bars[kBStageFree]);
       }
-      if (ok && graph) ok = mbar_wait(&bars[kBRqReady], 0, abort_flag, 902);
-      if (ok) ok = mbar_wait_spin(&bars[kBKFull], 0, abort_flag, 903);
-      if (ok) {
+      __syncwarp();
+    }
+    // hand-off 2: R~_q scaled and K(0) landed -> S(0)
+    ok = pair_rendezvous(kDqHandoffBar, ok);
+    if (ok) {
+      tc_fence_after();
+      if (leader) issue_s(0);
+      __syncwarp();
+    }
+    // hand-off 3: V(0) landed -> dP(0)
+    ok = pair_rendezvous(kDqHandoffBar, ok);
+    if (ok) {
+      tc_fence_after();
+      if (leader) issue_dp(0);
+      __syncwarp();
+    }
+    for (int j = 0; ok && j < n_tiles; ++j) {
+      // the warps have read S(j) and K(j+1) landed: next tile's S (it overlaps their dS work)
+      ok = pair_rendezvous(kDqHandoffBar, ok);
+      if (!ok) break;
+      if (j + 1 < n_tiles) {
         tc_fence_after();
-        issue_s(0);
-        ok = mbar_wait_spin(&bars[kBVFull], 0, abort_flag, 907);
-        if (ok) {
-          tc_fence_after();
-          issue_dp(0);
-        }
+        if (leader) issue_s(j + 1);
+        __syncwarp();
       }
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        // next tile's S as soon as the warps have read S (it overlaps their dS work)
-        if (!mbar_wait_spin(&bars[kBSRead], j & 1, abort_flag, 904)) break;
-        if (j + 1 < n_tiles) {
-          const int s1 = (j + 1) % kDqStages;
-          if (!mbar_wait_spin(&bars[kBKFull + s1], ((j + 1) / kDqStages) & 1, abort_flag, 905)) break;
-          tc_fence_after();
-          issue_s(j + 1);
-        }
-        // [dQ | dS R_k] += dS [K | R_k], then the next dP.  Both waits come
-        // before the two MMA groups: a wait issued behind queued MMAs only
-        // returns once the tensor pipe has nearly drained them.
-        if (!mbar_wait_spin(&bars[kBDsReady], j & 1, abort_flag, 906)) break;
-        if (j + 1 < n_tiles &&
-            !mbar_wait_spin(&bars[kBVFull + (j + 1) % kDqStages], ((j + 1) / kDqStages) & 1, abort_flag, 908))
-          break;
-        tc_fence_after();
+      // dS(j) written and V(j+1) landed: [dQ | dS R_k] += dS [K | R_k], then the next dP
+      ok = pair_rendezvous(kDqHandoffBar, ok);
+      if (!ok) break;
+      tc_fence_after();
+      if (leader) {
         const uint32_t sK = stage_k(j);
 #pragma unroll
         for (int kk = 0; kk < kQT / 16; ++kk)
@@ -1104,7 +1111,30 @@ __global__ void __launch_bounds__(kDqThreads, 1)
         // next tile's dP (overwrites dS, read in order above)
         if (j + 1 < n_tiles) issue_dp(j + 1);
       }
-      if (ok) mma_commit(&bars[kBAllDone]);
+      __syncwarp();
+    }
+    if (ok && leader) mma_commit(&bars[kBAllDone]);
+  } else if (warp == 10) {
+    // ------------------------------------------------------------ waiter for the MMA issuer
+    // Same hand-off sequence as warp 9; every wait of the issuer happens here.
+    bool ok = mbar_wait(&bars[kBQFull], 0, abort_flag, 901);
+    ok = pair_rendezvous(kDqHandoffBar, ok);
+    if (ok && graph) ok = mbar_wait(&bars[kBRqReady], 0, abort_flag, 902);
+    if (ok) ok = mbar_wait(&bars[kBKFull], 0, abort_flag, 903);
+    ok = pair_rendezvous(kDqHandoffBar, ok);
+    if (ok) ok = mbar_wait(&bars[kBVFull], 0, abort_flag, 907);
+    ok = pair_rendezvous(kDqHandoffBar, ok);
+    for (int j = 0; ok && j < n_tiles; ++j) {
+      ok = mbar_wait(&bars[kBSRead], j & 1, abort_flag, 904);
+      if (ok && j + 1 < n_tiles)
+        ok = mbar_wait(&bars[kBKFull + (j + 1) % kDqStages], ((j + 1) / kDqStages) & 1, abort_flag, 905);
+      ok = pair_rendezvous(kDqHandoffBar, ok);
+      if (!ok) break;
+      ok = mbar_wait(&bars[kBDsReady], j & 1, abort_flag, 906);
+      if (ok && j + 1 < n_tiles)
+        ok = mbar_wait(&bars[kBVFull + (j + 1) % kDqStages], ((j + 1) / kDqStages) & 1, abort_flag, 908);
+      ok = pair_rendezvous(kDqHandoffBar, ok);
+      if (!ok) break;
     }
   } else {
     // ------------------------------------------------------------ softmax-gradient warps 0-7 (query rows)

@@ -141,6 +141,29 @@ __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, v
   return mbar_spin_slow(bar, parity, abort_flag, site);
 }
 
+// Rendezvous of two whole warps on hardware named barrier `id` (64 threads);
+// returns the AND of the `ok` values both warps pass.  This is how an
+// MMA-issuing warp learns that its operands are ready from a waiter warp that
+// does the mbarrier waits for it: a barrier instruction does not queue behind
+// the calling warp's own outstanding tcgen05.mma instructions, whereas a
+// shared- or global-memory access from that warp does (measured on B200: an
+// mbarrier test on an already completed phase, issued behind queued MMAs,
+// leaves the tensor pipe idle for 80-180 cycles; this rendezvous costs about
+// 20).  Both warps must execute the same sequence of rendezvous; the AND
+// carries an abort from the waiter to the issuer at the same point.
+__device__ __forceinline__ bool pair_rendezvous(uint32_t id, bool ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "barrier.cta.red.and.aligned.pred q, %2, 64, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"(ok ? 1u : 0u), "r"(id)
+      : "memory");
+  return r != 0;
+}
+
 // ---------------------------------------------------------------------------
 // TMA (bulk tensor copies, global -> shared, no multicast)
 // ---------------------------------------------------------------------------
