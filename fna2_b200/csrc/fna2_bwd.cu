@@ -601,7 +601,8 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA stream 1: S^T, dP^T
-    if (lane == 0) {
+    // The whole warp runs the loop and its waits; an elected lane issues each group.
+    {
       constexpr uint32_t idesc_st = make_idesc_bf16(128, QT, 0, 0);  // S^T, dP^T (N = QT queries)
       const uint32_t r_layout = r_layout_of(RP);
       const uint32_t r_sbo = 8 * RP * 2;
@@ -616,32 +617,38 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
             !mbar_wait_spin(&bars[kARkReady], (it / n_it) & 1, abort_flag, 502))
           return false;
         tc_fence_after();
-        const uint32_t sQ = stage_q(it);
+        if (elect_one()) {
+          const uint32_t sQ = stage_q(it);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          mma_ss(tS, make_sdesc(sK + (kk >> 2) * L::kKChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B),
-                 make_sdesc(sQ + (kk >> 2) * L::kQChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B), idesc_st, kk > 0);
-        if (graph_of(it)) {
-          const uint32_t sRq = sQ + (D / 64) * L::kQChunk;
+          for (int kk = 0; kk < D / 16; ++kk)
+            mma_ss(tS, make_sdesc(sK + (kk >> 2) * L::kKChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B),
+                   make_sdesc(sQ + (kk >> 2) * L::kQChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B), idesc_st, kk > 0);
+          if (graph_of(it)) {
+            const uint32_t sRq = sQ + (D / 64) * L::kQChunk;
 #pragma unroll
-          for (int kk = 0; kk < RP / 16; ++kk)
-            mma_ss(tS, make_sdesc(sRk + kk * 32, 16, r_sbo, r_layout), make_sdesc(sRq + kk * 32, 16, 1024, kSwizzle128B),
-                   idesc_st, 1);
-          if ((it % n_it) == n_it - 1) mma_commit(&bars[kARkEmpty]);  // last use of this head's R_k
+            for (int kk = 0; kk < RP / 16; ++kk)
+              mma_ss(tS, make_sdesc(sRk + kk * 32, 16, r_sbo, r_layout),
+                     make_sdesc(sRq + kk * 32, 16, 1024, kSwizzle128B), idesc_st, 1);
+            if ((it % n_it) == n_it - 1) mma_commit(&bars[kARkEmpty]);  // last use of this head's R_k
+          }
+          mma_commit(&bars[kASFull]);
         }
-        mma_commit(&bars[kASFull]);
+        __syncwarp();
         return true;
       };
       auto issue_dp = [&](int it) -> bool {  // dP^T = V dO^T
         if (!mbar_wait_spin(&bars[kADoFull + (it & 1)], (it >> 1) & 1, abort_flag, 505)) return false;
         tc_fence_after();
-        const uint32_t sDo = smem_u32(smem + L::oDo + (it & 1) * L::kDoStage);
+        if (elect_one()) {
+          const uint32_t sDo = smem_u32(smem + L::oDo + (it & 1) * L::kDoStage);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          mma_ss(tDP, make_sdesc(sV + (kk >> 2) * L::kKChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B),
-                 make_sdesc(sDo + (kk >> 2) * L::kQChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B), idesc_st, kk > 0);
-        mma_commit(&bars[kADPFull]);
-        mma_commit(&bars[kADoEmpty + (it & 1)]);
+          for (int kk = 0; kk < D / 16; ++kk)
+            mma_ss(tDP, make_sdesc(sV + (kk >> 2) * L::kKChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B),
+                   make_sdesc(sDo + (kk >> 2) * L::kQChunk + (kk & 3) * 32, 16, 1024, kSwizzle128B), idesc_st, kk > 0);
+          mma_commit(&bars[kADPFull]);
+          mma_commit(&bars[kADoEmpty + (it & 1)]);
+        }
+        __syncwarp();
         return true;
       };
       bool ok = mbar_wait(&bars[kAKV], 0, abort_flag, 501) && issue_s(0) && issue_dp(0);
@@ -652,7 +659,8 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
     }
   } else if (warp == 11) {
     // ------------------------------------------------------------ MMA stream 2: dV, dK
-    if (lane == 0) {
+    // The whole warp runs the loop and its waits; an elected lane issues each group.
+    {
       constexpr uint32_t idesc_dv = make_idesc_bf16(128, D, 0, 1);        // dV (A in TMEM, B MN-major)
       constexpr uint32_t idesc_dk = make_idesc_bf16(128, D, 0, 1);        // dK only (vanilla heads)
       constexpr uint32_t idesc_dkr = make_idesc_bf16(128, D + RP, 0, 1);  // [dK | dR_k]
@@ -665,24 +673,30 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
         if (!mbar_wait_spin(&bars[kAPReady], it & 1, abort_flag, 506)) break;
         tc_fence_after();
         const uint32_t sDo = stage_do(it), sQ = stage_q(it);
+        if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < QT / 16; ++kk)
-          mma_ts(tDV, tPT + 8 * kk, make_sdesc(sDo + kk * 2048, L::kQChunk, 1024, kSwizzle128B), idesc_dv,
-                 (it > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(&bars[kADvDone]);
-        mma_commit(&bars[kADoEmpty + (it & 1)]);
+          for (int kk = 0; kk < QT / 16; ++kk)
+            mma_ts(tDV, tPT + 8 * kk, make_sdesc(sDo + kk * 2048, L::kQChunk, 1024, kSwizzle128B), idesc_dv,
+                   (it > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&bars[kADvDone]);
+          mma_commit(&bars[kADoEmpty + (it & 1)]);
+        }
+        __syncwarp();
         // [dK | dR_k] += dS^T [Q | R_q]
         if (!mbar_wait_spin(&bars[kADsReady], it & 1, abort_flag, 507)) break;
         tc_fence_after();
+        if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < QT / 16; ++kk)
-          mma_ts(tDK, tPT + 8 * kk, make_sdesc(sQ + kk * 2048, L::kQChunk, 1024, kSwizzle128B),
-                 graph ? idesc_dkr : idesc_dk, (it > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(&bars[kADkDone]);
-        mma_commit(&bars[kAQEmpty + it % L::kQStages]);
-        if (graph && (it % n_it) == n_it - 1 && it + 1 < total_it) mma_commit(&bars[kAHeadDone]);
+          for (int kk = 0; kk < QT / 16; ++kk)
+            mma_ts(tDK, tPT + 8 * kk, make_sdesc(sQ + kk * 2048, L::kQChunk, 1024, kSwizzle128B),
+                   graph ? idesc_dkr : idesc_dk, (it > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&bars[kADkDone]);
+          mma_commit(&bars[kAQEmpty + it % L::kQStages]);
+          if (graph && (it % n_it) == n_it - 1 && it + 1 < total_it) mma_commit(&bars[kAHeadDone]);
+        }
+        __syncwarp();
       }
-      if (ok) mma_commit(&bars[kAAllDone]);
+      if (ok && elect_one()) mma_commit(&bars[kAAllDone]);
     }
   } else {
     // ------------------------------------------------------------ softmax-gradient warps 0-7
@@ -1022,10 +1036,10 @@ __global__ void __launch_bounds__(kDqThreads, 1)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
-    // The whole warp follows the hand-off sequence below; lane 0 issues.  It
+    // The whole warp follows the hand-off sequence below; an elected lane
+    // issues each group.  It
     // learns that operands are ready only through pair_rendezvous with the
     // waiter warp (warp 10), so it never touches memory behind its queued MMAs.
-    const bool leader = lane == 0;
     constexpr uint32_t idesc_s = make_idesc_bf16(128, kQT, 0, 0);       // S, dP (N = 112 keys)
     constexpr uint32_t idesc_dq = make_idesc_bf16(128, D, 0, 1);        // dQ only (vanilla heads)
     constexpr uint32_t idesc_dqr = make_idesc_bf16(128, D + RP, 0, 1);  // [dQ | dS R_k]
@@ -1062,7 +1076,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
     bool ok = pair_rendezvous(kDqHandoffBar, true);
     if (ok) {
       tc_fence_after();
-      if (leader) {
+      if (elect_one()) {
         const uint32_t sQ = smem_u32(smem + L::oV), sDo = sQ + L::kQStage;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -1078,14 +1092,14 @@ __global__ void __launch_bounds__(kDqThreads, 1)
     ok = pair_rendezvous(kDqHandoffBar, ok);
     if (ok) {
       tc_fence_after();
-      if (leader) issue_s(0);
+      if (elect_one()) issue_s(0);
       __syncwarp();
     }
     // hand-off 3: V(0) landed -> dP(0)
     ok = pair_rendezvous(kDqHandoffBar, ok);
     if (ok) {
       tc_fence_after();
-      if (leader) issue_dp(0);
+      if (elect_one()) issue_dp(0);
       __syncwarp();
     }
     for (int j = 0; ok && j < n_tiles; ++j) {
@@ -1094,14 +1108,14 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       if (!ok) break;
       if (j + 1 < n_tiles) {
         tc_fence_after();
-        if (leader) issue_s(j + 1);
+        if (elect_one()) issue_s(j + 1);
         __syncwarp();
       }
       // dS(j) written and V(j+1) landed: [dQ | dS R_k] += dS [K | R_k], then the next dP
       ok = pair_rendezvous(kDqHandoffBar, ok);
       if (!ok) break;
       tc_fence_after();
-      if (leader) {
+      if (elect_one()) {
         const uint32_t sK = stage_k(j);
 #pragma unroll
         for (int kk = 0; kk < kQT / 16; ++kk)
@@ -1113,7 +1127,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       }
       __syncwarp();
     }
-    if (ok && leader) mma_commit(&bars[kBAllDone]);
+    if (ok && elect_one()) mma_commit(&bars[kBAllDone]);
   } else if (warp == 10) {
     // ------------------------------------------------------------ waiter for the MMA issuer
     // Same hand-off sequence as warp 9; every wait of the issuer happens here.

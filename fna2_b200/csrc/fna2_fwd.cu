@@ -233,7 +233,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the loop and its waits; an elected lane issues each group.
+    {
       constexpr uint32_t idesc_s = make_idesc_bf16(kBlockM, kBlockN, 0, 0);
       constexpr uint32_t idesc_pv = make_idesc_bf16(kBlockM, D, 0, 1);
       constexpr uint32_t r_layout = RP == 16 ? kSwizzle32B : (RP == 32 ? kSwizzle64B : kSwizzle128B);
@@ -274,9 +275,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
       if (ok) ok = wait_k(0);
       if (ok) {
+        if (elect_one()) {
 #pragma unroll
-        for (int i = 0; i < kFwdTiles; ++i)
-          if (n_t[i] > 0) issue_s(i, 0);
+          for (int i = 0; i < kFwdTiles; ++i)
+            if (n_t[i] > 0) issue_s(i, 0);
+        }
+        __syncwarp();
       }
       for (int j = 0; ok && j < n_kv; ++j) {
         const int b = j & 1;
@@ -292,17 +296,21 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t tO = tmem + 128 * i;
-          const uint32_t tP = tmem + 256 + 128 * i;
+          if (elect_one()) {
+            const uint32_t tO = tmem + 128 * i;
+            const uint32_t tP = tmem + 256 + 128 * i;
 #pragma unroll
-          for (int kk = 0; kk < kBlockN / 16; ++kk)
-            mma_ts(tO, tP + kk * 8, make_sdesc(sV + kk * 2048, L::kChunk, 1024, kSwizzle128B), idesc_pv,
-                   (j > 0 || kk > 0) ? 1u : 0u);
-          if (j + 1 < n_t[i]) issue_s(i, j + 1);
+            for (int kk = 0; kk < kBlockN / 16; ++kk)
+              mma_ts(tO, tP + kk * 8, make_sdesc(sV + kk * 2048, L::kChunk, 1024, kSwizzle128B), idesc_pv,
+                     (j > 0 || kk > 0) ? 1u : 0u);
+            if (j + 1 < n_t[i]) issue_s(i, j + 1);
+          }
+          __syncwarp();
         }
-        mma_commit(&bars[kBarVEmpty + b]);
+        if (elect_one()) mma_commit(&bars[kBarVEmpty + b]);
+        __syncwarp();
       }
-      if (ok) mma_commit(&bars[kBarAllDone]);
+      if (ok && elect_one()) mma_commit(&bars[kBarAllDone]);
     }
   } else {
     // ------------------------------------------------------------ softmax (warpgroup i = query tile i)

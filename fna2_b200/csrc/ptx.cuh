@@ -141,6 +141,22 @@ __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, v
   return mbar_spin_slow(bar, parity, abort_flag, site);
 }
 
+// True in exactly one lane of the calling warp, which must be converged.  The
+// MMA-issuing warps run their loops with all 32 lanes and issue each group of
+// tcgen05 instructions from the lane this selects: measured on B200 with busy
+// warps on the same scheduler, a group issued from an `if (lane == 0)` branch
+// kept the tensor pipe at about a third of the rate of the same group issued
+// under elect.sync from a converged warp (the operands stay warp-uniform).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .b32 rx;\n\t.reg .pred px;\n\t"
+      "elect.sync rx|px, 0xffffffff;\n\t"
+      "@px mov.s32 %0, 1;\n\t}\n"
+      : "+r"(pred));
+  return pred != 0;
+}
+
 // Rendezvous of two whole warps on hardware named barrier `id` (64 threads);
 // returns the AND of the `ok` values both warps pass.  This is how an
 // MMA-issuing warp learns that its operands are ready from a waiter warp that
