@@ -12,7 +12,7 @@ from typing import Optional
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("FNA2_LIB", os.path.join(HERE, "libfna2_b200.so"))
 
-FNA2_ABI_VERSION = 4
+FNA2_ABI_VERSION = 5
 FNA2_OK = 0
 FNA2_ERR_INVALID = -1
 FNA2_ERR_CUDA = -2
@@ -20,7 +20,7 @@ FNA2_ERR_WORKSPACE = -3
 
 EXPORTED = ["fna2_fwd", "fna2_bwd", "fna2_bwd_workspace_size", "fna2_last_error", "fna2_device_status",
             "fna2_abi_version", "fna2_bwd_noalloc", "fna2_qk_prep_fwd", "fna2_qk_prep_bwd", "fna2_decode", "fna2_decode_workspace_size",
-            "fna2_debug_watchdog", "fna2_fwd_workspace_size"]
+            "fna2_debug_watchdog", "fna2_fwd_workspace_size", "fna2_gemm"]
 FNA2_DTYPE_F32 = 0
 FNA2_DTYPE_BF16 = 1
 NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024  # FNA2_NOALLOC_SCRATCH_BYTES
@@ -151,6 +151,16 @@ class Fna2DecodeArgs(ctypes.Structure):
     ]
 
 
+class Fna2GemmArgs(ctypes.Structure):
+    _fields_ = [
+        ("m", _I64), ("n", _I64), ("k", _I64),
+        ("a", ctypes.c_void_p), ("lda", _I64), ("a_mn_major", ctypes.c_int32),
+        ("b", ctypes.c_void_p), ("ldb", _I64), ("b_mn_major", ctypes.c_int32),
+        ("c", ctypes.c_void_p), ("ldc", _I64), ("c_dtype", ctypes.c_int32),
+        ("split_k", ctypes.c_int32),
+    ]
+
+
 _lib: Optional[ctypes.CDLL] = None
 
 
@@ -188,6 +198,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.fna2_device_status.restype = ctypes.c_int
     lib.fna2_debug_watchdog.argtypes = [ctypes.c_int, ctypes.c_ulonglong]
     lib.fna2_debug_watchdog.restype = ctypes.c_int
+    lib.fna2_gemm.argtypes = [ctypes.POINTER(Fna2GemmArgs), ctypes.c_void_p]
+    lib.fna2_gemm.restype = ctypes.c_int
     lib.fna2_abi_version.argtypes = []
     lib.fna2_abi_version.restype = ctypes.c_int
     v = lib.fna2_abi_version()

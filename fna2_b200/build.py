@@ -16,7 +16,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libfna2_b200.so")
 SOURCES = ["fna2_api.cu"]
-DEPS = ["fna2_api.cu", "fna2_fwd.cu", "fna2_bwd.cu", "fna2_noalloc.cu", "fna2_qkprep.cu", "fna2_decode.cu", "fna2_kernels.cuh", "ptx.cuh"]
+DEPS = ["fna2_api.cu", "fna2_fwd.cu", "fna2_gemm.cu", "fna2_bwd.cu", "fna2_noalloc.cu", "fna2_qkprep.cu", "fna2_decode.cu", "fna2_kernels.cuh", "ptx.cuh"]
 HEADER = os.path.join(ROOT, "include", "fna2.h")
 
 

@@ -18,6 +18,7 @@
 
 #include "fna2_bwd.cu"
 #include "fna2_fwd.cu"
+#include "fna2_gemm.cu"
 #include "fna2_qkprep.cu"
 #include "fna2_decode.cu"
 
@@ -197,6 +198,54 @@ int map_r(CUtensorMap* m, const Fna2Tensor& t, const Shape& s, int rows, const c
 using namespace fna2;
 
 extern "C" int fna2_abi_version(void) { return FNA2_ABI_VERSION; }
+
+extern "C" int fna2_gemm(const Fna2GemmArgs* a, void* stream) {
+  g_last_error.clear();
+  FNA2_CHECK(a != nullptr, "null args");
+  FNA2_CHECK(a->m >= 1 && a->n >= 1 && a->k >= 1, "m, n, k must be >= 1 (got %lld, %lld, %lld)", (long long)a->m,
+             (long long)a->n, (long long)a->k);
+  FNA2_CHECK(a->m < (1ll << 31) && a->n < (1ll << 31) && a->k < (1ll << 31), "m, n, k must be < 2^31");
+  FNA2_CHECK(a->n % 32 == 0, "n must be a multiple of 32 (got %lld)", (long long)a->n);
+  FNA2_CHECK(a->c_dtype == FNA2_DTYPE_BF16 || a->c_dtype == FNA2_DTYPE_F32, "c_dtype must be bf16 or f32");
+  FNA2_CHECK(a->split_k >= 1 && a->split_k <= 4096, "split_k must be in [1, 4096]");
+  FNA2_CHECK(a->split_k == 1 || a->c_dtype == FNA2_DTYPE_F32, "split_k > 1 needs fp32 output");
+  FNA2_CHECK(a->a != nullptr && a->b != nullptr && a->c != nullptr, "null operand pointer");
+  FNA2_CHECK(((reinterpret_cast<uintptr_t>(a->a) | reinterpret_cast<uintptr_t>(a->b) | reinterpret_cast<uintptr_t>(a->c)) &
+              15u) == 0,
+             "operands must be 16-byte aligned");
+  FNA2_CHECK(a->lda % 8 == 0 && a->ldb % 8 == 0, "lda and ldb must be multiples of 8 elements");
+  FNA2_CHECK(a->ldc % (a->c_dtype == FNA2_DTYPE_F32 ? 4 : 8) == 0, "ldc must keep rows 16-byte aligned");
+  FNA2_CHECK(a->lda >= (a->a_mn_major ? a->m : a->k) && a->ldb >= (a->b_mn_major ? a->n : a->k) && a->ldc >= a->n,
+             "a leading dimension is smaller than its row");
+  CUtensorMap ta, tb;
+  // K-major: (k, rows) with 64 x tile-row boxes; MN-major: (rows, k) with 64 x 64 boxes
+  if (a->a_mn_major) {
+    if (int rc = make_map(&ta, a->a, a->m, a->k, 1, 1, a->lda, 0, 0, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B, "a")) return rc;
+  } else {
+    if (int rc = make_map(&ta, a->a, a->k, a->m, 1, 1, a->lda, 0, 0, 64, kGemmBM, CU_TENSOR_MAP_SWIZZLE_128B, "a"))
+      return rc;
+  }
+  if (a->b_mn_major) {
+    if (int rc = make_map(&tb, a->b, a->n, a->k, 1, 1, a->ldb, 0, 0, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B, "b")) return rc;
+  } else {
+    if (int rc = make_map(&tb, a->b, a->k, a->n, 1, 1, a->ldb, 0, 0, 64, kGemmBN, CU_TENSOR_MAP_SWIZZLE_128B, "b"))
+      return rc;
+  }
+  GemmParams p;
+  p.M = a->m;
+  p.N = a->n;
+  p.K = a->k;
+  p.a_mn = a->a_mn_major ? 1 : 0;
+  p.b_mn = a->b_mn_major ? 1 : 0;
+  p.c = a->c;
+  p.ldc = a->ldc;
+  p.c_f32 = a->c_dtype == FNA2_DTYPE_F32 ? 1 : 0;
+  p.chunks = static_cast<int>((a->k + kGemmBK - 1) / kGemmBK);
+  const int split = a->split_k < p.chunks ? a->split_k : p.chunks;
+  p.chunks_per_split = (p.chunks + split - 1) / split;
+  FNA2_CUDA(launch_gemm(ta, tb, p, split, static_cast<cudaStream_t>(stream)));
+  return FNA2_OK;
+}
 
 extern "C" const char* fna2_last_error(void) { return g_last_error.c_str(); }
 

@@ -50,7 +50,7 @@
 extern "C" {
 #endif
 
-#define FNA2_ABI_VERSION 4
+#define FNA2_ABI_VERSION 5
 
 #define FNA2_OK 0
 #define FNA2_ERR_INVALID (-1)
@@ -275,6 +275,32 @@ int fna2_device_status(int reset);
  * works.  fna2_debug_watchdog(0, 0) restores normal operation.  Synchronises
  * the current device. */
 int fna2_debug_watchdog(int withhold_site, unsigned long long wait_limit_ns);
+
+/* Dense bf16 GEMM for the stacked R_q / R_k projection (replaces the two
+ * nn.Linear layers rel_q_proj / rel_k_proj of FNA2/attention_fna2.py:320-335
+ * and the products autograd forms for them):
+ *   c_dtype == FNA2_DTYPE_BF16:  C[m][n]  = sum_k A[m][k] B[n][k]   (stored)
+ *   c_dtype == FNA2_DTYPE_F32:   C[m][n] += sum_k A[m][k] B[n][k]   (added; K may be
+ *                                split over split_k CTA slices; C is not cleared)
+ * A is bf16, K-major (A[m][k] at a[m*lda + k]) or, with a_mn_major = 1,
+ * M-major (A[m][k] at a[k*lda + m]); B likewise with N.  fp32 accumulation.
+ * Requirements: m, n, k >= 1; n a multiple of 32; 16-byte aligned a, b, c;
+ * lda, ldb multiples of 8 elements and ldc of 8 (bf16) or 4 (fp32) elements;
+ * split_k >= 1, and 1 for bf16 output.  FNA2_ERR_INVALID otherwise. */
+typedef struct Fna2GemmArgs {
+  int64_t m, n, k;
+  const void* a;
+  int64_t lda;
+  int32_t a_mn_major;
+  const void* b;
+  int64_t ldb;
+  int32_t b_mn_major;
+  void* c;
+  int64_t ldc;
+  int32_t c_dtype;
+  int32_t split_k;
+} Fna2GemmArgs;
+int fna2_gemm(const Fna2GemmArgs* args, void* stream);
 
 /* FNA2_ABI_VERSION of the loaded library. */
 int fna2_abi_version(void);
