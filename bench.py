@@ -32,9 +32,9 @@ against the measured copy bandwidth, with the decode oracle
 (oracle/decode_oracle.py) timed on the host beside it.
 
 ``--op rel_proj`` measures the fused R_q/R_k projection (fna2_b200/rel_proj.py:
-one cuBLAS GEMM over the stacked weights, strided views out) forward + backward
-on the workload's tokens (x [T, H*D] bf16), with the reference's two-Linear
-composition timed on the same GPU beside it.
+the library's tcgen05 GEMM over the stacked weights for Y, dX and dW, strided
+views out) forward + backward on the workload's tokens (x [T, H*D] bf16), with
+the reference's two-Linear composition timed on the same GPU beside it.
 """
 from __future__ import annotations
 
@@ -819,7 +819,7 @@ def run_decode(args, w):
 
 
 def run_rel_proj(args, w):
-    """Fused R_q/R_k projection (one GEMM over the stacked weights) fwd + bwd, one GPU."""
+    """Fused R_q/R_k projection (fna2_gemm over the stacked weights) fwd + bwd, one GPU."""
     import torch.nn.functional as F
     from fna2_b200.rel_proj import compute_rq_rk
     dev = "cuda"
@@ -872,12 +872,13 @@ def run_rel_proj(args, w):
     if peak is None:
         peak, peak_src = 1590.0, "fallback"
     print(json.dumps({
-        "metric": "R_q/R_k projection fwd+bwd TFLOP/s (bf16, one GEMM over the stacked weights)",
+        "metric": "R_q/R_k projection fwd+bwd TFLOP/s (bf16, fna2_gemm over the stacked weights)",
         "value": tf, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": w["desc"] + f"; x [T, {E}] bf16, H_G = {H}, R = {R}", "tokens": T,
                    "reference_two_linears_ms": ms_ref, "speedup_vs_reference_composition": ms_ref / ms,
-                   "gemm": "cuBLAS via torch (plain library GEMM)"},
+                   "gemm": "fna2_gemm (tcgen05, 128 x 256 tiles, persistent; Y, dX and dW)",
+                   "gpu_launches_per_step": 3},
         "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
                      "peak_source": peak_src},
         "clocks": clk,

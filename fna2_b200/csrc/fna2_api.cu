@@ -243,7 +243,12 @@ extern "C" int fna2_gemm(const Fna2GemmArgs* a, void* stream) {
   p.chunks = static_cast<int>((a->k + kGemmBK - 1) / kGemmBK);
   const int split = a->split_k < p.chunks ? a->split_k : p.chunks;
   p.chunks_per_split = (p.chunks + split - 1) / split;
-  FNA2_CUDA(launch_gemm(ta, tb, p, split, static_cast<cudaStream_t>(stream)));
+  p.tiles_n = static_cast<int>((a->n + kGemmBN - 1) / kGemmBN);
+  const int64_t tiles = p.tiles_n * ((a->m + kGemmBM - 1) / kGemmBM);
+  FNA2_CHECK(tiles * split < (1ll << 31), "too many output tiles");
+  p.tiles = static_cast<int>(tiles);
+  p.items = p.tiles * split;
+  FNA2_CUDA(launch_gemm(ta, tb, p, static_cast<cudaStream_t>(stream)));
   return FNA2_OK;
 }
 

@@ -7,16 +7,21 @@
 //   forward  Y  = X W^T      A = X  (K-major)   B = W  (K-major)   C bf16
 //   dX       dX = dY W       A = dY (K-major)   B = W  (MN-major)  C bf16
 //   dW       dW = dY^T X     A = dY (MN-major)  B = X  (MN-major)  C fp32, split over K
-// The dW product reduces over all T tokens: CTAs take slices of K and add their
-// fp32 partial tiles into C (zeroed by the caller) with red.global.add.
+// The dW product reduces over all T tokens: with fp32 output the K range may
+// be split into slices (work items ordered slice-major, so that the CTAs
+// running together read the same K chunks and share them in L2), and the
+// partial tiles are added into C (the caller clears it) with red.global.add.
 //
-// One CTA per 128 x 256 output tile (and K slice): warp 0 loads 64-deep K
-// chunks of A and B by TMA into a 4-stage ring (48 KB per stage, SW128), warp 1
-// issues four M=128, N=256, K=16 MMAs per chunk under elect.sync, warp 2 waits
-// on the ring's mbarriers for it and meets it at a named-barrier rendezvous (a
-// memory access of the issuing warp would wait behind its queued MMAs), warps
-// 3-6 read the 256 accumulator columns out of TMEM and store them.  All waits
-// are bounded.
+// Persistent: each CTA takes work items (128 x 256 output tile, K slice)
+// round-robin, output tiles N-fastest so that the CTAs running together share
+// A's rows in L2.  Warp 0 loads 64-deep K chunks of A and B by TMA into a
+// 4-stage ring (48 KB per stage, SW128) that runs on across items; warp 1
+// issues four M=128, N=256, K=16 MMAs per chunk under elect.sync into one of
+// two TMEM accumulators (256 columns each), so that the next item's MMAs run
+// while warps 3-6 drain the previous item's accumulator to global memory;
+// warp 2 performs every mbarrier wait of the issuer and meets it at a
+// named-barrier rendezvous (a memory access of the issuing warp would wait
+// behind its queued MMAs).  All waits are bounded.
 #pragma once
 
 #include "fna2_kernels.cuh"
@@ -36,17 +41,41 @@ struct GemmParams {
   int c_f32;       // 0: store bf16; 1: add fp32 partials (split over K)
   int chunks;      // 64-deep K chunks in total
   int chunks_per_split;
+  int tiles_n, tiles;  // output tiles along N, in total
+  int items;           // tiles x K slices, taken round-robin by the CTAs
 };
 
 struct GemmSmem {
   static constexpr int kABytes = kGemmBM * kGemmBK * 2;  // 16 KB
   static constexpr int kBBytes = kGemmBN * kGemmBK * 2;  // 32 KB
   static constexpr int kStage = kABytes + kBBytes;
-  static constexpr int oBar = kGemmStages * kStage;
-  static constexpr int kNumBars = 2 * kGemmStages + 1;
+  static constexpr int oStaging = kGemmStages * kStage;  // 4 KB per epilogue warp
+  static constexpr int oBar = oStaging + 4 * 4096;
+  static constexpr int kNumBars = 2 * kGemmStages + 4;   // full, empty, acc_full[2], acc_empty[2]
   static constexpr int oMisc = oBar + kNumBars * 8;
   static constexpr int kTotal = oMisc + 16 + 1024;
   static_assert(kTotal <= kMaxDynamicSmem, "shared memory budget");
+};
+
+// The CTA's work items (output tile, K slice) in order -- blockIdx.x,
+// +gridDim.x, ... over slice-major items -- skipping empty slices; every role
+// walks the same sequence.
+struct GemmWalk {
+  int pos;
+  __device__ explicit GemmWalk(const GemmParams&) : pos(static_cast<int>(blockIdx.x)) {}
+  __device__ bool next(const GemmParams& p, int64_t& m0, int64_t& n0, int& c0, int& nc) {
+    for (; pos < p.items; pos += gridDim.x) {
+      const int z = pos / p.tiles, tile = pos % p.tiles;
+      c0 = z * p.chunks_per_split;
+      nc = min(p.chunks, c0 + p.chunks_per_split) - c0;
+      if (nc <= 0) continue;
+      n0 = static_cast<int64_t>(tile % p.tiles_n) * kGemmBN;
+      m0 = static_cast<int64_t>(tile / p.tiles_n) * kGemmBM;
+      pos += gridDim.x;
+      return true;
+    }
+    return false;
+  }
 };
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -55,34 +84,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   using L = GemmSmem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::oBar);  // full[s], empty[s], acc_full
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::oBar);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kGemmStages;
+  uint64_t* acc_full = bars + 2 * kGemmStages;
+  uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::oMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::oMisc + 4);
   const int warp = warp_id(), lane = lane_id();
-  const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kGemmBN, m0 = static_cast<int64_t>(blockIdx.y) * kGemmBM;
-  const int c_begin = blockIdx.z * p.chunks_per_split;
-  const int c_end = min(p.chunks, c_begin + p.chunks_per_split);
-  const int n_chunks = c_end - c_begin;
-  if (n_chunks <= 0) {  // an empty K slice adds nothing (bf16 output is never split)
-    if (!p.c_f32) {
-      for (int i = threadIdx.x; i < kGemmBM * kGemmBN; i += blockDim.x) {
-        const int64_t m = m0 + i / kGemmBN, n = n0 + i % kGemmBN;
-        if (m < p.M && n < p.N) static_cast<__nv_bfloat16*>(p.c)[m * p.ldc + n] = __float2bfloat16(0.f);
-      }
-    }
-    return;
-  }
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < kGemmStages; ++s) {
-      mbar_init(&bars[s], 1);
-      mbar_init(&bars[kGemmStages + s], 1);
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
     }
-    mbar_init(&bars[2 * kGemmStages], 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -95,24 +119,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB);
-      for (int i = 0; i < n_chunks; ++i) {
-        const int s = i % kGemmStages;
-        if (i >= kGemmStages &&
-            !mbar_wait(&bars[kGemmStages + s], ((i / kGemmStages) - 1) & 1, abort_flag, 1401))
-          break;
-        uint8_t* sa = smem + s * L::kStage;
-        uint8_t* sb = sa + L::kABytes;
-        const int k0 = (c_begin + i) * kGemmBK;
-        mbar_expect_tx(&bars[s], L::kStage);
-        if (p.a_mn) {  // two 64-column (M) x 64-row (K) boxes
-          for (int h = 0; h < 2; ++h) tma_load_4d(sa + h * 8192, &tmA, &bars[s], static_cast<int>(m0) + 64 * h, k0, 0, 0);
-        } else {  // one 64-column (K) x 128-row (M) box
-          tma_load_4d(sa, &tmA, &bars[s], k0, static_cast<int>(m0), 0, 0);
-        }
-        if (p.b_mn) {
-          for (int h = 0; h < 4; ++h) tma_load_4d(sb + h * 8192, &tmB, &bars[s], static_cast<int>(n0) + 64 * h, k0, 0, 0);
-        } else {
-          tma_load_4d(sb, &tmB, &bars[s], k0, static_cast<int>(n0), 0, 0);
+      int g = 0;  // chunks loaded so far (ring position)
+      bool ok = true;
+      GemmWalk wk(p);
+      int64_t m0, n0;
+      int c0, nc;
+      while (ok && wk.next(p, m0, n0, c0, nc)) {
+        for (int c = 0; c < nc; ++c, ++g) {
+          const int s = g % kGemmStages;
+          if (g >= kGemmStages && !mbar_wait(&empty[s], ((g / kGemmStages) - 1) & 1, abort_flag, 1401)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + s * L::kStage;
+          uint8_t* sb = sa + L::kABytes;
+          const int k0 = (c0 + c) * kGemmBK;
+          mbar_expect_tx(&full[s], L::kStage);
+          if (p.a_mn) {  // two 64-column (M) x 64-row (K) boxes
+            for (int h = 0; h < 2; ++h) tma_load_4d(sa + h * 8192, &tmA, &full[s], static_cast<int>(m0) + 64 * h, k0, 0, 0);
+          } else {  // one 64-column (K) x 128-row (M) box
+            tma_load_4d(sa, &tmA, &full[s], k0, static_cast<int>(m0), 0, 0);
+          }
+          if (p.b_mn) {
+            for (int h = 0; h < 4; ++h) tma_load_4d(sb + h * 8192, &tmB, &full[s], static_cast<int>(n0) + 64 * h, k0, 0, 0);
+          } else {
+            tma_load_4d(sb, &tmB, &full[s], k0, static_cast<int>(n0), 0, 0);
+          }
         }
       }
     }
@@ -122,50 +154,73 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // The whole warp follows the hand-off sequence; an elected lane issues.
     const uint32_t idesc = make_idesc_bf16(kGemmBM, kGemmBN, p.a_mn, p.b_mn);
     bool ok = true;
-    for (int i = 0; i < n_chunks; ++i) {
-      ok = pair_rendezvous(kGemmHandoffBar, ok);  // chunk i landed
-      if (!ok) break;
-      tc_fence_after();
-      const int s = i % kGemmStages;
-      const uint32_t sa = smem_u32(smem + s * L::kStage), sb = sa + L::kABytes;
-      uint64_t ad[4], bd[4];
+    int g = 0, it = 0;
+    GemmWalk wk(p);
+    int64_t m0, n0;
+    int c0, nc;
+    while (ok && wk.next(p, m0, n0, c0, nc)) {
+      const int b = it & 1;
+      const uint32_t tacc = tmem + 256 * b;
+      for (int c = 0; c < nc; ++c, ++g) {
+        // chunk g landed (and, for the first chunk, accumulator b drained)
+        ok = pair_rendezvous(kGemmHandoffBar, ok);
+        if (!ok) break;
+        tc_fence_after();
+        const int s = g % kGemmStages;
+        const uint32_t sa = smem_u32(smem + s * L::kStage), sb = sa + L::kABytes;
+        uint64_t ad[4], bd[4];
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        ad[kk] = p.a_mn ? make_sdesc(sa + kk * 2048, 8192, 1024, kSwizzle128B) : make_sdesc(sa + kk * 32, 16, 1024, kSwizzle128B);
-        bd[kk] = p.b_mn ? make_sdesc(sb + kk * 2048, 8192, 1024, kSwizzle128B) : make_sdesc(sb + kk * 32, 16, 1024, kSwizzle128B);
-      }
-      if (elect_one()) {
+        for (int kk = 0; kk < 4; ++kk) {
+          ad[kk] = p.a_mn ? make_sdesc(sa + kk * 2048, 8192, 1024, kSwizzle128B) : make_sdesc(sa + kk * 32, 16, 1024, kSwizzle128B);
+          bd[kk] = p.b_mn ? make_sdesc(sb + kk * 2048, 8192, 1024, kSwizzle128B) : make_sdesc(sb + kk * 32, 16, 1024, kSwizzle128B);
+        }
+        if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) mma_ss(tmem, ad[kk], bd[kk], idesc, (i > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(&bars[kGemmStages + s]);
-        if (i == n_chunks - 1) mma_commit(&bars[2 * kGemmStages]);
+          for (int kk = 0; kk < 4; ++kk) mma_ss(tacc, ad[kk], bd[kk], idesc, (c > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&empty[s]);
+          if (c == nc - 1) mma_commit(&acc_full[b]);
+        }
+        __syncwarp();
       }
-      __syncwarp();
+      ++it;
     }
   } else if (warp == 2) {
     // ------------------------------------------------------------ waiter for the issuer
     bool ok = true;
-    for (int i = 0; i < n_chunks; ++i) {
-      if (ok) ok = mbar_wait(&bars[i % kGemmStages], (i / kGemmStages) & 1, abort_flag, 1402);
-      ok = pair_rendezvous(kGemmHandoffBar, ok);
-      if (!ok) break;
+    int g = 0, it = 0;
+    GemmWalk wk(p);
+    int64_t m0, n0;
+    int c0, nc;
+    while (ok && wk.next(p, m0, n0, c0, nc)) {
+      for (int c = 0; c < nc; ++c, ++g) {
+        if (ok && c == 0 && it >= 2) ok = mbar_wait(&acc_empty[it & 1], ((it >> 1) - 1) & 1, abort_flag, 1404);
+        if (ok) ok = mbar_wait(&full[g % kGemmStages], (g / kGemmStages) & 1, abort_flag, 1402);
+        ok = pair_rendezvous(kGemmHandoffBar, ok);
+        if (!ok) break;
+      }
+      ++it;
     }
   } else {
     // ------------------------------------------------------------ epilogue (warps 3-6)
     const int q = warp & 3;  // TMEM lane quadrant = rows [32q, 32q+32)
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    if (mbar_wait(&bars[2 * kGemmStages], 0, abort_flag, 1403)) {
+    uint8_t* stage = smem + L::oStaging + (warp - 3) * 4096;
+    int it = 0;
+    GemmWalk wk(p);
+    int64_t m0, n0;
+    int c0, nc;
+    while (wk.next(p, m0, n0, c0, nc)) {
+      const int b = it & 1;
+      if (!mbar_wait(&acc_full[b], (it >> 1) & 1, abort_flag, 1403)) break;
       tc_fence_after();
       const int64_t row0 = m0 + 32 * q;
       const int nvalid = static_cast<int>(p.M - row0 < 32 ? p.M - row0 : 32);
-      // staging through the (now idle) ring, 4 KB per warp
-      uint8_t* stage = smem + (warp - 3) * 4096;
 #pragma unroll 1
       for (int c = 0; c < kGemmBN / 32; ++c) {
         const int64_t col0 = n0 + 32 * c;
         if (col0 >= p.N) break;
         uint32_t v[32];
-        tmem_ld32(tmem + lane_base + 32 * c, v);
+        tmem_ld32(tmem + 256 * b + lane_base + 32 * c, v);
         tmem_ld_wait32(v);
         if (!p.c_f32) {
           uint32_t pk[16];
@@ -185,6 +240,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           __syncwarp();
         }
       }
+      // accumulator b may take item it+2
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      ++it;
     }
   }
 
@@ -192,16 +252,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
-inline cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int split,
-                               cudaStream_t stream) {
+inline cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(fna2_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmSmem::kTotal);
   if (e != cudaSuccess) return e;
-  const dim3 grid(static_cast<unsigned>((p.N + kGemmBN - 1) / kGemmBN), static_cast<unsigned>((p.M + kGemmBM - 1) / kGemmBM),
-                  static_cast<unsigned>(split));
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = p.items < sms ? p.items : sms;
   fna2_gemm_kernel<<<grid, kGemmThreads, GemmSmem::kTotal, stream>>>(a, b, p);
   return cudaGetLastError();
 }

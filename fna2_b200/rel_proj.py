@@ -13,7 +13,7 @@ takes directly (any 16-byte aligned strides): no permute copy, no contiguous()
 copy.  For bf16 inputs on the GPU the three products -- Y = X W^T, dX = dY W
 and dW = dY^T X -- run on the library's own tcgen05 GEMM (fna2_gemm in
 libfna2_b200.so: operands read K-major or MN-major in place, so no transposed
-copies; dW reduces over all tokens in fp32 split over CTA slices).  Other
+copies; dW reduces over all tokens in fp32 within one CTA per output tile).  Other
 dtypes and CPU tensors use torch.nn.functional.linear.  Values equal the
 reference's (the same dot products with fp32 accumulation, rounded once to
 `dtype`).
@@ -74,10 +74,7 @@ class _StackedProjection(torch.autograd.Function):
             _gemm(gy, False, w, True, T, E, N, gx)
         if ctx.needs_input_grad[1]:  # dW[j][e] = sum_t dY[t][j] X[t][e]: both read M/N-major in place
             gw32 = torch.zeros(N, E, device=x2.device, dtype=torch.float32)
-            tiles = math.ceil(E / 256) * math.ceil(N / 128)
-            sms = torch.cuda.get_device_properties(x2.device).multi_processor_count
-            split = max(1, min(math.ceil(2 * sms / tiles), math.ceil(T / 64)))
-            _gemm(gy, True, x2, True, N, E, T, gw32, split)
+            _gemm(gy, True, x2, True, N, E, T, gw32)  # one CTA per output tile, over all tokens
             gw = gw32.to(w.dtype)
         return gx, gw
 

@@ -281,7 +281,8 @@ int fna2_debug_watchdog(int withhold_site, unsigned long long wait_limit_ns);
  * and the products autograd forms for them):
  *   c_dtype == FNA2_DTYPE_BF16:  C[m][n]  = sum_k A[m][k] B[n][k]   (stored)
  *   c_dtype == FNA2_DTYPE_F32:   C[m][n] += sum_k A[m][k] B[n][k]   (added; K may be
- *                                split over split_k CTA slices; C is not cleared)
+ *                                split into split_k slices reduced with fp32 atomics;
+ *                                C is not cleared)
  * A is bf16, K-major (A[m][k] at a[m*lda + k]) or, with a_mn_major = 1,
  * M-major (A[m][k] at a[k*lda + m]); B likewise with N.  fp32 accumulation.
  * Requirements: m, n, k >= 1; n a multiple of 32; 16-byte aligned a, b, c;
