@@ -222,13 +222,14 @@ extern "C" int fna2_gemm(const Fna2GemmArgs* a, void* stream) {
   if (a->a_mn_major) {
     if (int rc = make_map(&ta, a->a, a->m, a->k, 1, 1, a->lda, 0, 0, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B, "a")) return rc;
   } else {
-    if (int rc = make_map(&ta, a->a, a->k, a->m, 1, 1, a->lda, 0, 0, 64, kGemmBM, CU_TENSOR_MAP_SWIZZLE_128B, "a"))
+    if (int rc = make_map(&ta, a->a, a->k, a->m, 1, 1, a->lda, 0, 0, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B, "a"))
       return rc;
   }
+  // each CTA of a pair loads 128 rows of A and 128 rows (output columns) of B per tile
   if (a->b_mn_major) {
     if (int rc = make_map(&tb, a->b, a->n, a->k, 1, 1, a->ldb, 0, 0, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B, "b")) return rc;
   } else {
-    if (int rc = make_map(&tb, a->b, a->k, a->n, 1, 1, a->ldb, 0, 0, 64, kGemmBN, CU_TENSOR_MAP_SWIZZLE_128B, "b"))
+    if (int rc = make_map(&tb, a->b, a->k, a->n, 1, 1, a->ldb, 0, 0, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B, "b"))
       return rc;
   }
   GemmParams p;
