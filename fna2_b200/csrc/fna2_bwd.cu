@@ -321,11 +321,13 @@ enum DkdvBar {
 constexpr int kDkdvThreads = 384;  // 8 softmax-gradient warps, producer, MMA (S/dP), prep, MMA (dV/dK)
 
 // P^T for one chunk of 32 query columns [qb, qb+32) of one key row:
-// exp2(S^T*c - LSE2), packed into pk[o .. o+16).  Columns outside [q_lo, q_hi)
-// (causal, sequence end) get exactly 0.
+// exp2(S^T*c - LSE2), packed into pk[o .. o+16); nl holds -LSE2 per query
+// column.  Columns outside [q_lo, q_hi) (causal, sequence end) get exactly 0.
+// The fp32 arithmetic runs two columns per packed instruction; each lane is
+// rounded as the scalar operation would be.
 template <int N>
 __device__ __forceinline__ void p_chunk_bwd(const uint32_t* sv_in, uint32_t* pk, const int qb, const int q_lo,
-                                            const int q_hi, const float* lv, const float sl2) {
+                                            const int q_hi, const float* nl, const float sl2) {
   uint32_t sv[N];
 #pragma unroll
   for (int k = 0; k < N; ++k) sv[k] = sv_in[k];
@@ -336,29 +338,32 @@ __device__ __forceinline__ void p_chunk_bwd(const uint32_t* sv_in, uint32_t* pk,
       if (!(qi >= q_lo && qi < q_hi)) sv[k] = __float_as_uint(-INFINITY);
     }
   }
+  const float2 c2 = make_float2(sl2, sl2);
 #pragma unroll
   for (int k = 0; k < N; k += 4) {
-    const float4 l4 = *reinterpret_cast<const float4*>(&lv[qb + k]);
-    pk[k >> 1] = pack_bf16(ex2(fmaf(__uint_as_float(sv[k]), sl2, -l4.x)),
-                           ex2(fmaf(__uint_as_float(sv[k + 1]), sl2, -l4.y)));
-    pk[(k >> 1) + 1] = pack_bf16(ex2(fmaf(__uint_as_float(sv[k + 2]), sl2, -l4.z)),
-                                 ex2(fmaf(__uint_as_float(sv[k + 3]), sl2, -l4.w)));
+    const float4 l4 = *reinterpret_cast<const float4*>(&nl[qb + k]);
+    const float2 e01 = __ffma2_rn(f32x2(sv[k], sv[k + 1]), c2, make_float2(l4.x, l4.y));
+    const float2 e23 = __ffma2_rn(f32x2(sv[k + 2], sv[k + 3]), c2, make_float2(l4.z, l4.w));
+    pk[k >> 1] = pack_bf16(ex2(e01.x), ex2(e01.y));
+    pk[(k >> 1) + 1] = pack_bf16(ex2(e23.x), ex2(e23.y));
   }
 }
 
 // dS^T = P^T (dP^T - Delta) for N columns starting at query column qb; P^T
-// packed bf16 in pk, result packed into dd.
+// packed bf16 in pk, nd holds -Delta per query column, result packed into dd.
 template <int N>
 __device__ __forceinline__ void ds_chunk_bwd(const uint32_t* pk, const uint32_t* dp, uint32_t* dd, const int qb,
-                                             const float* dv) {
+                                             const float* nd) {
 #pragma unroll
   for (int k = 0; k < N; k += 4) {
-    const float4 d4 = *reinterpret_cast<const float4*>(&dv[qb + k]);
+    const float4 d4 = *reinterpret_cast<const float4*>(&nd[qb + k]);
     const uint32_t a = pk[k >> 1], b = pk[(k >> 1) + 1];
-    dd[k >> 1] = pack_bf16(__uint_as_float(a << 16) * (__uint_as_float(dp[k]) - d4.x),
-                           __uint_as_float(a & 0xffff0000u) * (__uint_as_float(dp[k + 1]) - d4.y));
-    dd[(k >> 1) + 1] = pack_bf16(__uint_as_float(b << 16) * (__uint_as_float(dp[k + 2]) - d4.z),
-                                 __uint_as_float(b & 0xffff0000u) * (__uint_as_float(dp[k + 3]) - d4.w));
+    const float2 t01 = __fadd2_rn(f32x2(dp[k], dp[k + 1]), make_float2(d4.x, d4.y));
+    const float2 t23 = __fadd2_rn(f32x2(dp[k + 2], dp[k + 3]), make_float2(d4.z, d4.w));
+    const float2 r01 = __fmul2_rn(f32x2(a << 16, a & 0xffff0000u), t01);
+    const float2 r23 = __fmul2_rn(f32x2(b << 16, b & 0xffff0000u), t23);
+    dd[k >> 1] = pack_bf16(r01.x, r01.y);
+    dd[(k >> 1) + 1] = pack_bf16(r23.x, r23.y);
   }
 }
 
@@ -588,8 +593,8 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         if (lane + 32 * u < QT) {
-          lv[lane + 32 * u] = l2[u];
-          lv[QT + lane + 32 * u] = dl[u];
+          lv[lane + 32 * u] = -l2[u];  // -LSE2 and -Delta: addends of the packed fp32 ops
+          lv[QT + lane + 32 * u] = -dl[u];
         }
       }
       mbar_arrive(&bars[kAPrep + s]);
@@ -1162,6 +1167,8 @@ __global__ void __launch_bounds__(kDqThreads, 1)
     const float lse2 = row_ok ? p.ws_lse2[widx] : 0.f;
     const float delta = row_ok ? p.ws_delta[widx] : 0.f;
     const float sl2 = P.scale_log2;
+    // operands of the packed fp32 ops (two columns per instruction)
+    const float2 sl2x2 = make_float2(sl2, sl2), nlse2 = make_float2(-lse2, -lse2), ndelta = make_float2(-delta, -delta);
     const int limit = row_ok ? (P.causal ? min(si.len_k, q_local + 1) : si.len_k) : 0;
     bool ok = true;
     // raw R_q row for d_gs, fetched now and used in the epilogue
@@ -1205,7 +1212,11 @@ __global__ void __launch_bounds__(kDqThreads, 1)
               if (col0 + k >= limit) sv[k] = __float_as_uint(-INFINITY);
           }
 #pragma unroll
-          for (int k = 0; k < 32; ++k) pf[32 * c + k] = ex2(fmaf(__uint_as_float(sv[k]), sl2, -lse2));
+          for (int k = 0; k < 32; k += 2) {
+            const float2 e = __ffma2_rn(f32x2(sv[k], sv[k + 1]), sl2x2, nlse2);
+            pf[32 * c + k] = ex2(e.x);
+            pf[32 * c + k + 1] = ex2(e.y);
+          }
         } else {  // warpgroup 1, keys 96..111 of the tile
           tmem_ld16(tSw + 32, sv);
           tmem_ld_wait16(sv);
@@ -1215,7 +1226,11 @@ __global__ void __launch_bounds__(kDqThreads, 1)
               if (col0 + k >= limit) sv[k] = __float_as_uint(-INFINITY);
           }
 #pragma unroll
-          for (int k = 0; k < 16; ++k) pf[32 + k] = ex2(fmaf(__uint_as_float(sv[k]), sl2, -lse2));
+          for (int k = 0; k < 16; k += 2) {
+            const float2 e = __ffma2_rn(f32x2(sv[k], sv[k + 1]), sl2x2, nlse2);
+            pf[32 + k] = ex2(e.x);
+            pf[32 + k + 1] = ex2(e.y);
+          }
 #pragma unroll
           for (int k = 16; k < 32; ++k) pf[32 + k] = 0.f;
         }
@@ -1243,9 +1258,11 @@ __global__ void __launch_bounds__(kDqThreads, 1)
           for (int k = 16; k < 32; ++k) dp[k] = 0u;  // beyond the 112-column tile
         }
 #pragma unroll
-        for (int k = 0; k < 32; k += 2)
-          dd[16 * c + (k >> 1)] = pack_bf16(pf[32 * c + k] * (__uint_as_float(dp[k]) - delta),
-                                            pf[32 * c + k + 1] * (__uint_as_float(dp[k + 1]) - delta));
+        for (int k = 0; k < 32; k += 2) {
+          const float2 r = __fmul2_rn(make_float2(pf[32 * c + k], pf[32 * c + k + 1]),
+                                      __fadd2_rn(f32x2(dp[k], dp[k + 1]), ndelta));
+          dd[16 * c + (k >> 1)] = pack_bf16(r.x, r.y);
+        }
       }
       tmem_st32(tDPw, dd);  // columns this warp has already read
       tmem_st_wait();

@@ -452,6 +452,12 @@ __device__ __forceinline__ float lg2(float x) {
   asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// Two raw 32-bit words as the fp32 pair of a packed instruction (__ffma2_rn,
+// __fadd2_rn, __fmul2_rn: two fp32 lanes per instruction on sm_100, each lane
+// rounded exactly as the scalar operation).
+__device__ __forceinline__ float2 f32x2(uint32_t lo, uint32_t hi) {
+  return make_float2(__uint_as_float(lo), __uint_as_float(hi));
+}
 // Round two floats to bf16 (round-to-nearest-even) and pack them, lo in bits 0..15.
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   uint32_t r;
