@@ -320,13 +320,12 @@ enum DkdvBar {
 
 constexpr int kDkdvThreads = 384;  // 8 softmax-gradient warps, producer, MMA (S/dP), prep, MMA (dV/dK)
 
-// P^T for one chunk of 32 query columns [qb, qb+32) of one key row:
-// exp2(S^T*c - LSE2), packed into pk[o .. o+16); nl holds -LSE2 per query
-// column.  Columns outside [q_lo, q_hi) (causal, sequence end) get exactly 0.
+// P^T for one chunk of N query columns [qb, qb+N) of one key row:
+// exp2(S^T*c - LSE2) into pf[0 .. N); nl holds -LSE2 per query column.  Columns outside [q_lo, q_hi) (causal, sequence end) get exactly 0.
 // The fp32 arithmetic runs two columns per packed instruction; each lane is
 // rounded as the scalar operation would be.
 template <int N>
-__device__ __forceinline__ void p_chunk_bwd(const uint32_t* sv_in, uint32_t* pk, const int qb, const int q_lo,
+__device__ __forceinline__ void p_chunk_bwd(const uint32_t* sv_in, float* pf, const int qb, const int q_lo,
                                             const int q_hi, const float* nl, const float sl2) {
   uint32_t sv[N];
 #pragma unroll
@@ -344,24 +343,23 @@ __device__ __forceinline__ void p_chunk_bwd(const uint32_t* sv_in, uint32_t* pk,
     const float4 l4 = *reinterpret_cast<const float4*>(&nl[qb + k]);
     const float2 e01 = __ffma2_rn(f32x2(sv[k], sv[k + 1]), c2, make_float2(l4.x, l4.y));
     const float2 e23 = __ffma2_rn(f32x2(sv[k + 2], sv[k + 3]), c2, make_float2(l4.z, l4.w));
-    pk[k >> 1] = pack_bf16(ex2(e01.x), ex2(e01.y));
-    pk[(k >> 1) + 1] = pack_bf16(ex2(e23.x), ex2(e23.y));
+    pf[k] = ex2(e01.x), pf[k + 1] = ex2(e01.y), pf[k + 2] = ex2(e23.x), pf[k + 3] = ex2(e23.y);
   }
 }
 
-// dS^T = P^T (dP^T - Delta) for N columns starting at query column qb; P^T
-// packed bf16 in pk, nd holds -Delta per query column, result packed into dd.
+// dS^T = P^T (dP^T - Delta) for N columns starting at query column qb; P^T in
+// fp32 (as the reference forms dS), nd holds -Delta per query column, result
+// packed into dd.
 template <int N>
-__device__ __forceinline__ void ds_chunk_bwd(const uint32_t* pk, const uint32_t* dp, uint32_t* dd, const int qb,
+__device__ __forceinline__ void ds_chunk_bwd(const float* pf, const uint32_t* dp, uint32_t* dd, const int qb,
                                              const float* nd) {
 #pragma unroll
   for (int k = 0; k < N; k += 4) {
     const float4 d4 = *reinterpret_cast<const float4*>(&nd[qb + k]);
-    const uint32_t a = pk[k >> 1], b = pk[(k >> 1) + 1];
     const float2 t01 = __fadd2_rn(f32x2(dp[k], dp[k + 1]), make_float2(d4.x, d4.y));
     const float2 t23 = __fadd2_rn(f32x2(dp[k + 2], dp[k + 3]), make_float2(d4.z, d4.w));
-    const float2 r01 = __fmul2_rn(f32x2(a << 16, a & 0xffff0000u), t01);
-    const float2 r23 = __fmul2_rn(f32x2(b << 16, b & 0xffff0000u), t23);
+    const float2 r01 = __fmul2_rn(make_float2(pf[k], pf[k + 1]), t01);
+    const float2 r23 = __fmul2_rn(make_float2(pf[k + 2], pf[k + 3]), t23);
     dd[k >> 1] = pack_bf16(r01.x, r01.y);
     dd[(k >> 1) + 1] = pack_bf16(r23.x, r23.y);
   }
@@ -746,16 +744,21 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars[kASRead]);
-        uint32_t pk[QH / 2];
-        p_chunk_bwd<32>(sv, pk, qw, q_lo, q_hi, lv, sl2);
-        if constexpr (QH == 48) p_chunk_bwd<16>(sv + 32, pk + 16, qw + 32, q_lo, q_hi, lv, sl2);
+        float pf[QH];  // P^T in fp32: packed bf16 for the dV MMA, fp32 for dS^T
+        p_chunk_bwd<32>(sv, pf, qw, q_lo, q_hi, lv, sl2);
+        if constexpr (QH == 48) p_chunk_bwd<16>(sv + 32, pf + 32, qw + 32, q_lo, q_hi, lv, sl2);
         // the packed columns are free once the previous tile's dK has run
         if (it > 0 && !mbar_wait(&bars[kADkDone], (it - 1) & 1, abort_flag, 703)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        tmem_st_packed<QH / 2>(tPTw, pk);
+        {
+          uint32_t pk[QH / 2];
+#pragma unroll
+          for (int k = 0; k < QH / 2; ++k) pk[k] = pack_bf16(pf[2 * k], pf[2 * k + 1]);
+          tmem_st_packed<QH / 2>(tPTw, pk);
+        }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -776,7 +779,7 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars[kADpRead]);
-          ds_chunk_bwd<QH>(pk, dp, dd, qw, lv + QT);
+          ds_chunk_bwd<QH>(pf, dp, dd, qw, lv + QT);
           if (!mbar_wait(&bars[kADvDone], it & 1, abort_flag, 707)) {
             ok = false;
             break;
