@@ -147,6 +147,23 @@ int check_problem(const Fna2Problem& p, Shape* s) {
   return FNA2_OK;
 }
 
+// Grid order of the varlen kernels.  They launch one CTA per (table entry,
+// head); each sequence's entries are listed heaviest causal tile first.  With
+// the entry as the fast grid dimension (the default) the CTAs resident together
+// work on one head of one sequence and share its streamed K/V (or Q/dO) tiles
+// in L2, which matters when there are thousands of CTAs per SM.  On a small
+// problem the same order dispatches the last heads' heaviest tiles in the last
+// wave, and the kernel waits for them; with the head as the fast dimension
+// every head's heaviest tiles go first.  Small: at most kHeadFastTokenHeads
+// token-heads (rows x heads) and a table that fits the grid's y dimension.
+constexpr int64_t kHeadFastTokenHeads = 768 * 1024;
+bool head_fast_grid(const Shape& s) {
+  if (!s.varlen) return false;
+  const int64_t rows = s.Tq > s.Tk ? s.Tq : s.Tk;
+  const int64_t tab = (rows + 127) / 128 + s.B;  // longest table: one entry per 128-row tile, plus one per sequence
+  return rows * s.H <= kHeadFastTokenHeads && tab <= 65535;
+}
+
 ProblemDev to_dev(const Fna2Problem& p, const Shape& s) {
   ProblemDev d;
   d.heads = s.H;
@@ -160,6 +177,7 @@ ProblemDev to_dev(const Fna2Problem& p, const Shape& s) {
   d.total_k = s.varlen ? s.Tk : s.Sk;
   d.varlen = s.varlen ? 1 : 0;
   d.causal = s.varlen ? 1 : (p.causal ? 1 : 0);
+  d.head_fast = head_fast_grid(s) ? 1 : 0;
   d.cu_q = p.cu_seqlens_q;
   d.cu_k = p.cu_seqlens_k;
   d.scale = p.softmax_scale;

@@ -423,11 +423,12 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
   float* vec = reinterpret_cast<float*>(smem + L::oVec);
 
   const ProblemDev& P = p.prob;
-  const int hk = blockIdx.y;
+  const int hk = grid_head(P);
   int n_blk;
   SeqInfo si;
   if (P.varlen) {  // one CTA per real key tile (table written by the pre kernel)
-    const int4 e0 = p.tab_k[2 * blockIdx.x], e1 = p.tab_k[2 * blockIdx.x + 1];
+    const int te = grid_entry(P);
+    const int4 e0 = p.tab_k[2 * te], e1 = p.tab_k[2 * te + 1];
     if (e0.x < 0) return;
     n_blk = e0.x;
     si.q_start = e0.y, si.k_start = e0.z, si.len_q = e0.w, si.len_k = e1.x, si.b = 0;
@@ -930,11 +931,12 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::oMisc + 4);
 
   const ProblemDev& P = p.prob;
-  const int h = blockIdx.y;
+  const int h = grid_head(P);
   int m_blk;
   SeqInfo si;
   if (P.varlen) {  // one CTA per real query tile (table written by the pre kernel)
-    const int4 e0 = p.tab_q[2 * blockIdx.x], e1 = p.tab_q[2 * blockIdx.x + 1];
+    const int te = grid_entry(P);
+    const int4 e0 = p.tab_q[2 * te], e1 = p.tab_q[2 * te + 1];
     if (e0.x < 0) return;
     m_blk = e0.x;
     si.q_start = e0.y, si.k_start = e0.z, si.len_q = e0.w, si.len_k = e1.x, si.b = 0;
@@ -1362,6 +1364,7 @@ cudaError_t launch_bwd_t(const BwdMaps& m, const BwdParams& p, cudaStream_t stre
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
     if (e != cudaSuccess) return e;
     dim3 grid(p.prob.varlen ? p.tab_k_len : p.n_nblocks, p.prob.heads_kv, p.prob.varlen ? 1 : p.batch);
+    if (p.prob.varlen && p.prob.head_fast) grid = dim3(p.prob.heads_kv, p.tab_k_len, 1);
     kern<<<grid, kDkdvThreads, L::kTotal, stream>>>(m.qS, m.k, m.v, m.dOS, m.rqS, m.rk, p);
     e = cudaGetLastError();
     if (e == cudaSuccess && ev) e = cudaEventRecord(ev[2], stream);
@@ -1373,6 +1376,7 @@ cudaError_t launch_bwd_t(const BwdMaps& m, const BwdParams& p, cudaStream_t stre
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal);
     if (e != cudaSuccess) return e;
     dim3 grid(p.prob.varlen ? p.tab_q_len : p.n_mblocks, p.prob.heads, p.prob.varlen ? 1 : p.batch);
+    if (p.prob.varlen && p.prob.head_fast) grid = dim3(p.prob.heads, p.tab_q_len, 1);
     kern<<<grid, kDqThreads, L::kTotal, stream>>>(m.q, m.kDq, m.vDq, m.dO, m.rq, m.rkDq, p);
     e = cudaGetLastError();
     if (e == cudaSuccess && ev) e = cudaEventRecord(ev[3], stream);

@@ -114,8 +114,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   if (P.varlen) {
     // grid (table entry, head): one CTA per real pair of query tiles; the table
     // lists each sequence's pairs heaviest first, so the CTAs of one head and
-    // sequence run together and share its K/V tiles in L2
-    const int4 e0 = p.tab[2 * blockIdx.x], e1 = p.tab[2 * blockIdx.x + 1];
+    // sequence run together and share its K/V tiles in L2 (head_fast: the
+    // transposed grid of small problems)
+    const int te = grid_entry(P);
+    const int4 e0 = p.tab[2 * te], e1 = p.tab[2 * te + 1];
     if (e0.x < 0) return;
     pair = e0.x;
     si.q_start = e0.y, si.k_start = e0.z, si.len_q = e0.w, si.len_k = e1.x, si.b = 0;
@@ -123,7 +125,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     pair = (p.n_mblocks + 1) / 2 - 1 - static_cast<int>(blockIdx.x);
     si = seq_info(P, blockIdx.z);
   }
-  const int h = blockIdx.y;
+  const int h = grid_head(P);
   const int q0 = pair * 2 * kBlockM;
   if (q0 >= si.len_q) return;
   const int hk = h / (P.heads / P.heads_kv);
@@ -518,7 +520,9 @@ cudaError_t launch_fwd_t(const CUtensorMap& q, const CUtensorMap& k, const CUten
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
-  const dim3 grid = p.prob.varlen ? dim3(p.tab_len, grid_y, 1) : dim3((p.n_mblocks + 1) / 2, grid_y, grid_z);
+  const dim3 grid = !p.prob.varlen         ? dim3((p.n_mblocks + 1) / 2, grid_y, grid_z)
+                    : p.prob.head_fast ? dim3(grid_y, p.tab_len, 1)
+                                       : dim3(p.tab_len, grid_y, 1);
   kern<<<grid, kFwdThreads, L::kTotal, stream>>>(q, k, v, rq, rk, p);
   return cudaGetLastError();
 }

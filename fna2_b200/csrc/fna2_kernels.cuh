@@ -37,12 +37,22 @@ struct ProblemDev {
   int seqlen_q, seqlen_k;  // dense lengths; varlen: max lengths (grid sizing only)
   int total_q, total_k;    // varlen: rows of the packed q and k/v tensors
   int varlen, causal;
+  // varlen grids: 0 = (table entry, head), 1 = (head, table entry); see head_fast_grid
+  int head_fast;
   const int* cu_q;
   const int* cu_k;
   float scale;       // softmax_scale
   float scale_log2;  // softmax_scale * log2(e)
   const float* gs;   // graph_scale [H_G]
 };
+
+// Grid coordinates of a varlen kernel launched over (table entry, head): the
+// entry is the fast dimension unless p.head_fast (small problems), in which
+// case every head's heaviest tiles are dispatched before any lighter ones.
+__device__ __forceinline__ int grid_entry(const ProblemDev& p) { return p.head_fast ? blockIdx.y : blockIdx.x; }
+__device__ __forceinline__ int grid_head(const ProblemDev& p) {
+  return (p.varlen && p.head_fast) ? blockIdx.x : blockIdx.y;
+}
 
 __device__ __forceinline__ SeqInfo seq_info(const ProblemDev& p, int bz) {
   SeqInfo s;
