@@ -28,6 +28,8 @@
 // The rank-r bias is one extra K-slice (K = r_pad) of each score MMA, with one
 // side pre-scaled by gs/scale in shared memory (R~_k in the dK/dV kernel, R~_q
 // in the dQ kernel).
+#include <type_traits>
+
 #include "fna2_kernels.cuh"
 #include "ptx.cuh"
 
@@ -236,7 +238,7 @@ __device__ __forceinline__ uint32_t r_layout_of(int rp) {
 // ---------------------------------------------------------------------------
 // One CTA per (128-row key tile, KV head, sequence), looping over the query
 // heads of the GQA group and the causally visible query tiles of QT rows
-// (dkdv_query_rows: 96, or 64 for head_dim 128 with r_pad 32).
+// (dkdv_query_rows: 96, or 80 for head_dim 128 with r_pad 32).
 //
 // The bias enters the score MMA as R~_k R_q^T with R~_k = R_k*gs/scale, scaled
 // in shared memory once per head.  dR_k rides along with dK as extra
@@ -249,8 +251,8 @@ __device__ __forceinline__ uint32_t r_layout_of(int rp) {
 // columns, the next tile's S^T and dP^T can be computed as soon as the warps
 // have read this tile's S^T and dP^T.  P^T and dS^T share their columns: dS^T
 // is written once dV has read P^T, the next P^T once dK has read dS^T.
-// Per query tile (warpgroup w owns query columns [w*QT/2, (w+1)*QT/2), each
-// thread one key row = TMEM lane):
+// Per query tile (warpgroup 0 owns query columns [0, QH0), warpgroup 1
+// [QH0, QT); each thread one key row = TMEM lane):
 //   tensor core:  S^T = K Q^T (+ R~_k R_q^T), dP^T = V dO^T  (SS)
 //   warps:        P^T = exp2(S^T*c - LSE2) (bf16), dS^T = P^T (dP^T - Delta)
 //   tensor core:  dV += P^T dO, [dK | dR_k] += dS^T [Q | R_q]  (TS form)
@@ -261,10 +263,13 @@ __device__ __forceinline__ uint32_t r_layout_of(int rp) {
 template <int D, int RP>
 struct DkdvCfg {
   static constexpr int QT = dkdv_query_rows(D, RP);
-  static constexpr int QH = QT / 2;  // query columns per warpgroup
+  // query columns of warpgroup 0 ([0, QH0)) and 1 ([QH0, QT)): 32 or 48 each, so
+  // that every TMEM load and store of a warpgroup starts on a 16-column boundary
+  // of its region (80 = 48 + 32)
+  static constexpr int QH0 = QT >= 80 ? 48 : 32, QH1 = QT - QH0;
   static constexpr int tDV = 0, tDK = D, tS = 2 * D + RP, tDP = tS + QT, tPT = tDP + QT;
   static_assert(tPT + QT / 2 <= 512, "TMEM budget");
-  static_assert(QH == 32 || QH == 48, "warpgroup column split");
+  static_assert((QH0 == 32 || QH0 == 48) && (QH1 == 32 || QH1 == 48), "warpgroup column split");
 };
 
 template <int D, int RP>
@@ -365,17 +370,33 @@ __device__ __forceinline__ void ds_chunk_bwd(const float* pf, const uint32_t* dp
   }
 }
 
-// Store QH/2 packed columns (16 or 24) of this warp's lanes.
+// Store a warpgroup's NP packed columns (16, or 24 when it owns 48 query
+// columns) of this warp's lanes.
 template <int NP>
 __device__ __forceinline__ void tmem_st_packed(uint32_t taddr, const uint32_t* r) {
   tmem_st16(taddr, r);
   if constexpr (NP == 24) tmem_st8(taddr + 16, r + 16);
 }
 
-// dR_k of head h from the accumulator columns (minus the earlier heads' share).
+// Zero RP accumulator columns of this warp's lanes.
+template <int RP>
+__device__ __forceinline__ void tmem_zero_cols(uint32_t tcol) {
+  uint32_t z[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) z[i] = 0u;
+  if (RP == 16) {
+    tmem_st16(tcol, z);
+  } else {
+    tmem_st32(tcol, z);
+  }
+}
+
+// dR_k of head h from its accumulator columns (cleared at the start of each
+// graph head of a GQA group).
 template <int RP>
 __device__ __forceinline__ void store_drk(const BwdParams& p, const SeqInfo& si, int h, int64_t krow, bool kv_valid,
-                                          uint32_t tcol, const float* drk_prev, uint32_t* rv) {
+                                          uint32_t tcol) {
+  uint32_t rv[32];
   const ProblemDev& P = p.prob;
   const float gsh = __ldg(P.gs + h);  // dR_k = gs * dS^T R_q
   if (RP == 16) {
@@ -394,8 +415,7 @@ __device__ __forceinline__ void store_drk(const BwdParams& p, const SeqInfo& si,
         uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-          wp[i] = pack_bf16((__uint_as_float(rv[c + 2 * i]) - drk_prev[c + 2 * i]) * gsh,
-                            (__uint_as_float(rv[c + 2 * i + 1]) - drk_prev[c + 2 * i + 1]) * gsh);
+          wp[i] = pack_bf16(__uint_as_float(rv[c + 2 * i]) * gsh, __uint_as_float(rv[c + 2 * i + 1]) * gsh);
         *reinterpret_cast<uint4*>(dst + c) = w;
       }
     }
@@ -410,7 +430,7 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
                          const BwdParams p) {
   using L = DkdvSmem<D, RP>;
   using C = DkdvCfg<D, RP>;
-  constexpr int QT = C::QT, QH = C::QH;
+  constexpr int QT = C::QT;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   if ((smem - smem_raw) + L::kUsed > L::kTotal) {  // layout does not fit the launch's shared memory
@@ -704,110 +724,119 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax-gradient warps 0-7
-    const int wg = warp >> 2;  // warpgroup: query columns [QH*wg, QH*wg + QH)
+    const int wg = warp >> 2;  // warpgroup: query columns [0, QH0) or [QH0, QT)
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int t = tid & 127;   // key row within the tile (TMEM lane)
     const int kv_local = n0 + t;
     const bool kv_valid = kv_local < si.len_k;
     const float sl2 = P.scale_log2;
     const int64_t krow = si.k_start + kv_local;
-    const uint32_t tSw = tS + lane_base + QH * wg, tDPw = tDP + lane_base + QH * wg;
-    const uint32_t tPTw = tPT + lane_base + (QH / 2) * wg;
-    const int qw = QH * wg;  // first query column of this warpgroup
-    float drk_prev[RP];      // dR_k columns already stored for earlier heads
-#pragma unroll
-    for (int i = 0; i < RP; ++i) drk_prev[i] = 0.f;
+    const int qw = wg ? C::QH0 : 0;  // first query column of this warpgroup
+    // 48 query columns (else 32); a compile-time constant when both halves match
+    const bool wide = wg ? (C::QH1 == 48) : (C::QH0 == 48);
+    const uint32_t tSw = tS + lane_base + qw, tDPw = tDP + lane_base + qw;
+    const uint32_t tPTw = tPT + lane_base + qw / 2;
     int it = 0, hb = 0;
     bool ok = true;
-
-    for (int e = 0; ok && e < g; ++e) {
-      const int h = hk * g + e;
-      const bool graph = e < gh;
-      for (int mi = 0; mi < n_it; ++mi, ++it) {
-        const int s = it % L::kQStages;
-        const int m0 = (m_start + mi) * QT;
-        const float* lv = vec + s * 2 * QT;
-        // valid query columns q in [q_lo, q_hi) (tile-relative) for this key row
-        const int q_hi = kv_valid ? min(QT, si.len_q - m0) : 0;
-        const int q_lo = P.causal ? (kv_local - m0) : 0;
-        if (!mbar_wait(&bars[kAPrep + s], (it / L::kQStages) & 1, abort_flag, 702) ||
-            !mbar_wait(&bars[kASFull], it & 1, abort_flag, 701)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        // phase 1: read S^T, release it for the next tile, then P^T (packed bf16)
-        uint32_t sv[QH];
-        tmem_ld32(tSw, sv);
-        if constexpr (QH == 48) tmem_ld16(tSw + 32, sv + 32);
-        tmem_ld_wait32(sv);
-        if constexpr (QH == 48) tmem_ld_wait16(sv + 32);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[kASRead]);
-        float pf[QH];  // P^T in fp32: packed bf16 for the dV MMA, fp32 for dS^T
-        p_chunk_bwd<32>(sv, pf, qw, q_lo, q_hi, lv, sl2);
-        if constexpr (QH == 48) p_chunk_bwd<16>(sv + 32, pf + 32, qw + 32, q_lo, q_hi, lv, sl2);
-        // the packed columns are free once the previous tile's dK has run
-        if (it > 0 && !mbar_wait(&bars[kADkDone], (it - 1) & 1, abort_flag, 703)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        {
-          uint32_t pk[QH / 2];
-#pragma unroll
-          for (int k = 0; k < QH / 2; ++k) pk[k] = pack_bf16(pf[2 * k], pf[2 * k + 1]);
-          tmem_st_packed<QH / 2>(tPTw, pk);
-        }
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[kAPReady]);
-        // phase 2: read dP^T (releasing it for the next tile), dS^T = P^T (dP^T - Delta)
-        // into the packed columns once dV has read P^T from them
-        if (!mbar_wait(&bars[kADPFull], it & 1, abort_flag, 704)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        {
-          uint32_t dp[QH], dd[QH / 2];
-          tmem_ld32(tDPw, dp);
-          if constexpr (QH == 48) tmem_ld16(tDPw + 32, dp + 32);
-          tmem_ld_wait32(dp);
-          if constexpr (QH == 48) tmem_ld_wait16(dp + 32);
+    // the tile loop, compiled once per column width so that each warpgroup's
+    // arrays and loads are sized at compile time
+    auto tile_loop = [&](auto wide_tag) {
+      constexpr bool kWide = decltype(wide_tag)::value;
+      constexpr int QW = kWide ? 48 : 32;  // this warpgroup's query columns
+      for (int e = 0; ok && e < g; ++e) {
+        const int h = hk * g + e;
+        const bool graph = e < gh;
+        for (int mi = 0; mi < n_it; ++mi, ++it) {
+          const int s = it % L::kQStages;
+          const int m0 = (m_start + mi) * QT;
+          const float* lv = vec + s * 2 * QT;
+          // valid query columns q in [q_lo, q_hi) (tile-relative) for this key row
+          const int q_hi = kv_valid ? min(QT, si.len_q - m0) : 0;
+          const int q_lo = P.causal ? (kv_local - m0) : 0;
+          if (!mbar_wait(&bars[kAPrep + s], (it / L::kQStages) & 1, abort_flag, 702) ||
+              !mbar_wait(&bars[kASFull], it & 1, abort_flag, 701)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // phase 1: read S^T, release it for the next tile, then P^T (packed bf16)
+          uint32_t sv[QW];
+          tmem_ld32(tSw, sv);
+          if constexpr (kWide) tmem_ld16(tSw + 32, sv + 32);
+          tmem_ld_wait32(sv);
+          if constexpr (kWide) tmem_ld_wait16(sv + 32);
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&bars[kADpRead]);
-          ds_chunk_bwd<QH>(pf, dp, dd, qw, lv + QT);
-          if (!mbar_wait(&bars[kADvDone], it & 1, abort_flag, 707)) {
+          if (lane == 0) mbar_arrive(&bars[kASRead]);
+          float pf[QW];  // P^T in fp32: packed bf16 for the dV MMA, fp32 for dS^T
+          p_chunk_bwd<32>(sv, pf, qw, q_lo, q_hi, lv, sl2);
+          if constexpr (kWide) p_chunk_bwd<16>(sv + 32, pf + 32, qw + 32, q_lo, q_hi, lv, sl2);
+          // the packed columns are free once the previous tile's dK has run
+          if (it > 0 && !mbar_wait(&bars[kADkDone], (it - 1) & 1, abort_flag, 703)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          tmem_st_packed<QH / 2>(tPTw, dd);
-        }
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars[kADsReady]);
-        // GQA: at the end of a graph head that is followed by another head, store
-        // this head's dR_k columns (accumulated on top of the earlier heads')
-        if (wg == 0 && graph && mi == n_it - 1 && it + 1 < total_it) {
-          if (!mbar_wait(&bars[kAHeadDone], hb & 1, abort_flag, 705)) {
-            ok = false;
-            break;
-          }
-          ++hb;
-          tc_fence_after();
-          uint32_t rv[32];
-          store_drk<RP>(p, si, h, krow, kv_valid, tDK + lane_base + D, drk_prev, rv);
+          {
+            uint32_t pk[QW / 2];
 #pragma unroll
-          for (int i = 0; i < RP; ++i) drk_prev[i] = __uint_as_float(rv[i]);
+            for (int k = 0; k < QW / 2; ++k) pk[k] = pack_bf16(pf[2 * k], pf[2 * k + 1]);
+            tmem_st_packed<QW / 2>(tPTw, pk);
+          }
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars[kAPReady]);
+          // phase 2: read dP^T (releasing it for the next tile), dS^T = P^T (dP^T - Delta)
+          // into the packed columns once dV has read P^T from them
+          if (!mbar_wait(&bars[kADPFull], it & 1, abort_flag, 704)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          {
+            uint32_t dp[QW], dd[QW / 2];
+            tmem_ld32(tDPw, dp);
+            if constexpr (kWide) tmem_ld16(tDPw + 32, dp + 32);
+            tmem_ld_wait32(dp);
+            if constexpr (kWide) tmem_ld_wait16(dp + 32);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars[kADpRead]);
+            ds_chunk_bwd<QW>(pf, dp, dd, qw, lv + QT);
+            if (!mbar_wait(&bars[kADvDone], it & 1, abort_flag, 707)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            tmem_st_packed<QW / 2>(tPTw, dd);
+          }
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars[kADsReady]);
+          // GQA: at the end of a graph head that is followed by another head, store
+          // this head's dR_k columns and clear them for the next head (whose first
+          // dK MMA waits for this warpgroup's next dS^T arrival)
+          if (wg == 0 && graph && mi == n_it - 1 && it + 1 < total_it) {
+            if (!mbar_wait(&bars[kAHeadDone], hb & 1, abort_flag, 705)) {
+              ok = false;
+              break;
+            }
+            ++hb;
+            tc_fence_after();
+            store_drk<RP>(p, si, h, krow, kv_valid, tDK + lane_base + D);
+            tmem_zero_cols<RP>(tDK + lane_base + D);
+            tmem_st_wait();
+            tc_fence_before();
+          }
         }
       }
-    }
+    };
+    if (wide)
+      tile_loop(std::true_type{});
+    else
+      tile_loop(std::false_type{});
     if (ok && mbar_wait(&bars[kAAllDone], 0, abort_flag, 706)) {
       tc_fence_after();
       // each warpgroup stores half of the D columns of dV and dK
@@ -833,8 +862,7 @@ __global__ void __launch_bounds__(kDkdvThreads, 1)
       }
       if (wg == 0 && gh > 0 && gh == g) {
         // dR_k of the group's last head (a graph head; otherwise it was stored at its end)
-        uint32_t rv[32];
-        store_drk<RP>(p, si, hk * g + gh - 1, krow, kv_valid, tDK + lane_base + D, drk_prev, rv);
+        store_drk<RP>(p, si, hk * g + gh - 1, krow, kv_valid, tDK + lane_base + D);
       }
     }
   }

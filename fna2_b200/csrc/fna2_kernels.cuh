@@ -14,10 +14,11 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kEps = 1e-6f;  // O = acc/(l+1e-6), LSE = m + log(l+1e-6)  (flash_naylis_attn.py:192,195)
 
-// Query rows per tile of the key-stationary backward kernel: the largest
-// multiple of 32 for which dV, [dK | dR_k], S^T, dP^T and a separate packed
-// P^T fit in the 512 TMEM columns.
-__host__ __device__ constexpr int dkdv_query_rows(int D, int RP) { return (D == 128 && RP == 32) ? 64 : 96; }
+// Query rows per tile of the key-stationary backward kernel: the largest of
+// 96, 80 and 64 for which dV, [dK | dR_k], S^T, dP^T and a separate packed P^T
+// fit in the 512 TMEM columns (D + D + r_pad + 2.5 QT <= 512); the two
+// softmax warpgroups take 48 + 48, 48 + 32 or 32 + 32 query columns.
+__host__ __device__ constexpr int dkdv_query_rows(int D, int RP) { return (D == 128 && RP == 32) ? 80 : 96; }
 
 // Key rows per tile of the query-stationary (dQ) backward kernel: [dQ | dR_q]
 // (160 columns), S and dP (112 each; dS is written over dP's first columns),
